@@ -1,0 +1,797 @@
+// B200 (sm_100a) grouped GEMM for the MoE FFN path: persistent ragged-M / ragged-K tile
+// scheduler, TMA-fed tcgen05 UMMA with fp32 accumulators in TMEM (double-buffered so the
+// epilogue of tile i overlaps the mainloop of tile i+1), and four fused epilogues:
+//   MGF_EPI_BIAS        D = bf16(acc + bias[e])                     (down-proj fwd, dgrads)
+//   MGF_EPI_SWIGLU      aux = bf16(acc + bias[e]), D2 = clamped SwiGLU(aux)  (up-proj fwd)
+//   MGF_EPI_SWIGLU_BWD  D = SwiGLU_bwd(acc, aux)                    (down-proj dgrad)
+//   MGF_EPI_WGRAD       D[e] = A[g]^T B[g] over ragged K, D2[e] = column sums of B[g]
+//
+// Semantics follow Butterfingrz/CuTe-MoE-Train (paths relative to cutlass_op/bf16_grouped_mm/):
+//   bias epilogue          csrc/grouped_mm_kernel.cuh:130-143 (fp32 acc + bias, one bf16 rounding)
+//   SwiGLU forward         csrc/grouped_mm_swiglu_visitor.cuh:295-334 (gate = even column,
+//                          up = odd column, min() on gate, two-sided clamp on up,
+//                          out = g*sigmoid(alpha*g)*(u+1), computed from the bf16-rounded aux)
+//   SwiGLU backward        csrc/grouped_mm_swiglu_bwd_visitor.cuh:35-68
+//   ragged-K weight grad   csrc/grouped_mm_common.cuh:120-133
+//   bias gradient          custom_op.py:79-101 (_segment_sum_rows, fp32 accumulation)
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer (one elected thread)
+//   warp 1      TMEM allocator + UMMA issuer; for ragged-K it also patches the K tail of the
+//               last stage (zero rows past the group end) and writes the bias-gradient "ones" row
+//   warps 2..5  epilogue: TMEM -> registers -> fused math -> predicated global stores
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "moe_gemm.h"
+#include "ptx.cuh"
+
+namespace mgf {
+
+__device__ unsigned int g_status;
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kMaxGroups = 1024;
+constexpr int kNumEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kNumEpiWarps;
+constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s per pipeline wait
+constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
+
+template <int BN>
+struct TileCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + SCHED_BYTES;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct Params {
+  int epi;
+  int E;
+  int64_t total_rows;
+  int m, n, k;
+  int n_tiles;
+  int m_tiles;        // ragged-K: tiles along m per group (incl. the extra bias-grad tile)
+  int m_tiles_real;   // ragged-K: ceil(m / BM)
+  int bias_grad;      // ragged-K: write D2
+  const int32_t* offs;
+  const __nv_bfloat16* bias;
+  int64_t bias_stride;
+  __nv_bfloat16* d;
+  int64_t ldd, ldd_batch;
+  __nv_bfloat16* d2;
+  int64_t ldd2;
+  const __nv_bfloat16* aux;
+  int64_t ld_aux;
+  float alpha, limit;
+  int store_aux;
+};
+
+struct TileInfo {
+  int e;
+  int m_blk, n_blk;
+  int row0, row_end;      // ragged-M: global rows of this tile / group end
+  int k_start, k_end;     // ragged-K: token range of the group
+  int nk;                 // number of BK blocks
+};
+
+struct SchedSmem {
+  int* prefix;     // [E+1] tile prefix
+  int* seg_start;  // [E]
+  int* seg_end;    // [E]
+};
+
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             uint64_t limit_ns = kWaitLimitNs) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((++it & 127u) == 0) {
+      if (*abort_flag) return false;
+      if (ptx::globaltimer_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicOr(&g_status, MGF_DEV_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+template <bool RAGGED_K>
+__device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedSmem& s, TileInfo& ti) {
+  int lo = 0, hi = p.E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s.prefix[mid] <= t) lo = mid; else hi = mid;
+  }
+  ti.e = lo;
+  const int local = t - s.prefix[lo];
+  ti.m_blk = local / p.n_tiles;
+  ti.n_blk = local - ti.m_blk * p.n_tiles;
+  if constexpr (!RAGGED_K) {
+    ti.row0 = s.seg_start[lo] + ti.m_blk * BM;
+    ti.row_end = s.seg_end[lo];
+    ti.k_start = 0;
+    ti.k_end = p.k;
+    ti.nk = (p.k + BK - 1) / BK;
+  } else {
+    ti.row0 = 0;
+    ti.row_end = 0;
+    ti.k_start = s.seg_start[lo];
+    ti.k_end = s.seg_end[lo];
+    ti.nk = (ti.k_end - ti.k_start + BK - 1) / BK;
+  }
+}
+
+// Clamp every group's [start, end) into [0, total_rows] and build the tile prefix.  Malformed
+// offs (decreasing, negative, or past total_rows) are reported through g_status, never by a
+// trap; the clamped segments keep every access in bounds.  Run by one warp.
+template <int BN, bool RAGGED_K>
+__device__ void build_schedule(const Params& p, const SchedSmem& s, int lane) {
+  int running = 0;
+  bool bad = false;
+  const long long tr = p.total_rows;
+  for (int base = 0; base < p.E; base += 32) {
+    const int e = base + lane;
+    int cnt = 0;
+    if (e < p.E) {
+      const long long raw_prev = e == 0 ? 0 : (long long)__ldg(p.offs + e - 1);
+      const long long raw_end = (long long)__ldg(p.offs + e);
+      if (raw_end < raw_prev || raw_end > tr || raw_prev < 0) bad = true;
+      const long long sp = raw_prev < 0 ? 0 : (raw_prev > tr ? tr : raw_prev);
+      const long long ep = raw_end < sp ? sp : (raw_end > tr ? tr : raw_end);
+      s.seg_start[e] = (int)sp;
+      s.seg_end[e] = (int)ep;
+      if constexpr (!RAGGED_K) {
+        cnt = (int)((ep - sp + BM - 1) / BM) * p.n_tiles;
+      } else {
+        cnt = p.m_tiles * p.n_tiles;
+      }
+    }
+    int inc = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, inc, off);
+      if (lane >= off) inc += o;
+    }
+    if (e < p.E) s.prefix[e + 1] = running + inc;
+    running += __shfl_sync(0xffffffffu, inc, 31);
+  }
+  if (lane == 0) s.prefix[0] = 0;
+  if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&g_status, MGF_DEV_BAD_OFFS);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+__device__ __forceinline__ float sigmoidf_fast(float z) { return __fdividef(1.0f, 1.0f + __expf(-z)); }
+
+// SwiGLU forward on one (gate, up) pair of bf16-rounded values.
+__device__ __forceinline__ float swiglu_fwd(float g, float u, float alpha, float limit) {
+  const float gc = fminf(g, limit);
+  const float uc = fmaxf(fminf(u, limit), -limit);
+  return gc * sigmoidf_fast(alpha * gc) * (uc + 1.0f);
+}
+
+// SwiGLU backward for one packed (gate, up) word of aux; returns packed (d_gate, d_up).
+__device__ __forceinline__ uint32_t swiglu_bwd_word(float gs, uint32_t aux_word, float alpha, float limit) {
+  const float g = bf16_lo(aux_word);
+  const float u = bf16_hi(aux_word);
+  const float gc = fminf(g, limit);
+  const float uc = fmaxf(fminf(u, limit), -limit);
+  const float sig = sigmoidf_fast(alpha * gc);
+  float d_gate = gs * (uc + 1.0f) * sig * (1.0f + alpha * gc * (1.0f - sig));
+  float d_up = gs * gc * sig;
+  d_gate = (g <= limit) ? d_gate : 0.0f;
+  d_up = (u >= -limit && u <= limit) ? d_up : 0.0f;
+  return pack_bf16x2(d_gate, d_up);
+}
+
+template <int BN, int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const Params p) {
+  using Cfg = TileCfg<BN>;
+  constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
+  constexpr int STAGES = Cfg::STAGES;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
+  uint64_t* drain_bar = bars + 2 * STAGES + 4;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* sched = reinterpret_cast<int*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
+  SchedSmem ss{sched, sched + (kMaxGroups + 1), sched + 2 * (kMaxGroups + 1)};
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full_bar[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(ptx::smem_u32(&tfull_bar[b]), 1);
+      ptx::mbar_init(ptx::smem_u32(&tempty_bar[b]), kNumEpiWarps);
+    }
+    ptx::mbar_init(ptx::smem_u32(drain_bar), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  if (warp == 2) build_schedule<BN, RAGGED_K>(p, ss, lane);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int total_tiles = ss.prefix[p.E];
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_parity[STAGES];
+      bool outstanding[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) { outstanding[s] = false; issued_parity[s] = 0; }
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        TileInfo ti;
+        decode_tile<RAGGED_K>(t, p, ss, ti);
+        const int n0 = ti.n_blk * BN;
+        for (int kb = 0; kb < ti.nk; ++kb) {
+          if (!wait_bounded(ptx::smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag)) { ok = false; break; }
+          const uint32_t fb = ptx::smem_u32(&full_bar[stage]);
+          ptx::mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          const uint32_t sA = ptx::smem_u32(stage_base + stage * Cfg::STAGE_BYTES);
+          const uint32_t sB = sA + Cfg::A_BYTES;
+          if constexpr (!RAGGED_K) {
+            ptx::tma_load_2d(sA, &tmA, fb, kb * BK, ti.row0);
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c) ptx::tma_load_3d(sB + c * 8192, &tmB, fb, n0 + 64 * c, kb * BK, ti.e);
+            } else {
+              ptx::tma_load_3d(sB, &tmB, fb, kb * BK, n0, ti.e);
+            }
+          } else {
+            const int kr = ti.k_start + kb * BK;
+            const int m0 = ti.m_blk * BM;
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c) ptx::tma_load_2d(sA + c * 8192, &tmA, fb, m0 + 64 * c, kr);
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) ptx::tma_load_2d(sB + c * 8192, &tmB, fb, n0 + 64 * c, kr);
+          }
+          outstanding[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Stopped early: let the copies already in flight land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (outstanding[s]) wait_bounded(ptx::smem_u32(&full_bar[s]), issued_parity[s], abort_flag, kDrainLimitNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    constexpr uint32_t idesc = ptx::make_idesc_bf16(BM, BN, A_MN, B_MN);
+    constexpr uint32_t a_lbo = A_MN ? 8192u : 16u;
+    constexpr uint32_t b_lbo = B_MN ? 8192u : 16u;
+    constexpr uint32_t a_kstep = A_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
+    constexpr uint32_t b_kstep = B_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    bool issued_any = false;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++it) {
+      TileInfo ti;
+      decode_tile<RAGGED_K>(t, p, ss, ti);
+      const int buf = it & 1;
+      const uint32_t tph = (it >> 1) & 1;
+      ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tempty_bar[buf]), tph ^ 1, abort_flag));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      int ones_r = -1;
+      if constexpr (RAGGED_K) {
+        if (p.bias_grad) {
+          const int m0 = ti.m_blk * BM;
+          if (p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
+        }
+      }
+      for (int kb = 0; kb < ti.nk; ++kb) {
+        ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), phase, abort_flag));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        uint8_t* sA_ptr = stage_base + stage * Cfg::STAGE_BYTES;
+        if constexpr (RAGGED_K) {
+          const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
+          if (valid_k < BK || ones_r >= 0) {
+            // Zero the K rows past the group end (they hold the next group's tokens),
+            // in every 64-column chunk of A and B.  Each K row is one 128-byte line.
+            constexpr int kChunks = BM / 64 + BN / 64;
+            const int nrows = BK - valid_k;
+            const int n16 = nrows * 8 * kChunks;
+            for (int i = lane; i < n16; i += 32) {
+              const int chunk = i / (nrows * 8);
+              const int rem = i - chunk * nrows * 8;
+              const int row = valid_k + rem / 8;
+              const int col16 = rem & 7;
+              uint8_t* base = sA_ptr + chunk * 8192;  // A chunks then B chunks are contiguous
+              *reinterpret_cast<uint4*>(base + row * 128 + col16 * 16) = make_uint4(0, 0, 0, 0);
+            }
+            if (ones_r >= 0) {
+              // A feature row past m reads as zero (TMA out-of-bounds fill); set it to 1.0 for
+              // the valid K rows so accumulator row ones_r receives the column sums of B.
+              const int c1 = ones_r >> 6, mm = ones_r & 63;
+              for (int kr = lane; kr < valid_k; kr += 32) {
+                const int off = c1 * 8192 + kr * 128 + ((((mm >> 3) ^ (kr & 7))) << 4) + (mm & 7) * 2;
+                *reinterpret_cast<uint16_t*>(sA_ptr + off) = 0x3F80u;
+              }
+            }
+            ptx::fence_proxy_async_smem();
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {
+          const uint32_t sA = ptx::smem_u32(sA_ptr);
+          const uint32_t sB = sA + Cfg::A_BYTES;
+          const uint64_t adesc = ptx::make_smem_desc_sw128(sA, a_lbo, 1024);
+          const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit(ptx::smem_u32(&empty_bar[stage]));
+          issued_any = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (lane == 0) {
+        if (ti.nk > 0) ptx::umma_commit(ptx::smem_u32(&tfull_bar[buf]));
+        else ptx::mbar_arrive(ptx::smem_u32(&tfull_bar[buf]));
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0 && issued_any) {
+      // Stopped early: wait for the UMMAs already issued before TMEM is released.
+      ptx::umma_commit(ptx::smem_u32(drain_bar));
+      wait_bounded(ptx::smem_u32(drain_bar), 0, abort_flag, kDrainLimitNs);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+      TileInfo ti;
+      decode_tile<RAGGED_K>(t, p, ss, ti);
+      const int buf = it & 1;
+      const uint32_t tph = (it >> 1) & 1;
+      if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
+      ptx::tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      const int n0 = ti.n_blk * BN;
+
+      if constexpr (!RAGGED_K) {
+        const int grow = ti.row0 + r;
+        const bool warp_active = ti.row0 + q * 32 < ti.row_end;
+        const bool valid = grow < ti.row_end;
+        if (warp_active) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            const int col0 = n0 + c * 32;
+            if (col0 >= p.n) break;
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(tbase + c * 32, v);
+            ptx::tmem_ld_wait();
+            if (!valid) continue;
+            if constexpr (EPI == MGF_EPI_BIAS || EPI == MGF_EPI_SWIGLU) {
+              float f[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+              if (p.bias != nullptr) {
+                const uint4* bp = reinterpret_cast<const uint4*>(p.bias + (int64_t)ti.e * p.bias_stride + col0);
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                  if (col0 + 8 * g < p.n) {
+                    const uint4 bw = __ldg(bp + g);
+                    const uint32_t w[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                      f[8 * g + 2 * h] += bf16_lo(w[h]);
+                      f[8 * g + 2 * h + 1] += bf16_hi(w[h]);
+                    }
+                  }
+                }
+              }
+              uint32_t packed[16];
+#pragma unroll
+              for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(f[2 * h], f[2 * h + 1]);
+              if (EPI == MGF_EPI_BIAS || p.store_aux) {
+                uint4* dp = reinterpret_cast<uint4*>(p.d + (int64_t)grow * p.ldd + col0);
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                  if (col0 + 8 * g < p.n)
+                    dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+              }
+              if constexpr (EPI == MGF_EPI_SWIGLU) {
+                uint32_t so[8];
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                  const float a0 = swiglu_fwd(bf16_lo(packed[2 * h]), bf16_hi(packed[2 * h]), p.alpha, p.limit);
+                  const float a1 =
+                      swiglu_fwd(bf16_lo(packed[2 * h + 1]), bf16_hi(packed[2 * h + 1]), p.alpha, p.limit);
+                  so[h] = pack_bf16x2(a0, a1);
+                }
+                uint4* sp = reinterpret_cast<uint4*>(p.d2 + (int64_t)grow * p.ldd2 + (col0 >> 1));
+#pragma unroll
+                for (int g = 0; g < 2; ++g)
+                  if (col0 + 16 * g < p.n) sp[g] = make_uint4(so[4 * g], so[4 * g + 1], so[4 * g + 2], so[4 * g + 3]);
+              }
+            } else if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
+              const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * col0);
+              uint4* gp = reinterpret_cast<uint4*>(p.d + (int64_t)grow * p.ldd + 2 * col0);
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                if (col0 + 4 * g < p.n) {
+                  const uint4 aw = __ldg(ap + g);
+                  uint4 o;
+                  o.x = swiglu_bwd_word(__uint_as_float(v[4 * g + 0]), aw.x, p.alpha, p.limit);
+                  o.y = swiglu_bwd_word(__uint_as_float(v[4 * g + 1]), aw.y, p.alpha, p.limit);
+                  o.z = swiglu_bwd_word(__uint_as_float(v[4 * g + 2]), aw.z, p.alpha, p.limit);
+                  o.w = swiglu_bwd_word(__uint_as_float(v[4 * g + 3]), aw.w, p.alpha, p.limit);
+                  gp[g] = o;
+                }
+              }
+            }
+          }
+        }
+      } else {
+        // ragged-K weight gradient: rows are output features m0 + r
+        const int m0 = ti.m_blk * BM;
+        const int frow = m0 + r;
+        int ones_r = -1;
+        if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
+        const bool row_out = frow < p.m;
+        const bool row_bias = (r == ones_r);
+        const bool warp_active = (m0 + q * 32 < p.m) || (ones_r >= q * 32 && ones_r < q * 32 + 32);
+        if (warp_active) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            const int col0 = n0 + c * 32;
+            if (col0 >= p.n) break;
+            uint32_t packed[16];
+            if (ti.nk > 0) {
+              uint32_t v[32];
+              ptx::tmem_ld_32x32b_x32(tbase + c * 32, v);
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(__uint_as_float(v[2 * h]), __uint_as_float(v[2 * h + 1]));
+            } else {
+#pragma unroll
+              for (int h = 0; h < 16; ++h) packed[h] = 0u;
+            }
+            uint4* dp = nullptr;
+            if (row_out) dp = reinterpret_cast<uint4*>(p.d + (int64_t)ti.e * p.ldd_batch + (int64_t)frow * p.ldd + col0);
+            else if (row_bias) dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
+            if (dp != nullptr) {
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                if (col0 + 8 * g < p.n)
+                  dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&tempty_bar[buf]));
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ============================================================================ host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                        const uint32_t* box) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t d[3];
+  cuuint64_t s[2];
+  cuuint32_t b[3];
+  cuuint32_t e[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+};
+
+static DeviceInfo device_info(int dev) {
+  static DeviceInfo cache[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (dev < 0 || dev >= 64) return DeviceInfo{};
+  if (cache[dev].sms == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return cache[dev];
+}
+
+template <int BN, int EPI, bool A_MN, bool B_MN>
+static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid, cudaStream_t st) {
+  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN>;
+  constexpr int smem = TileCfg<BN>::SMEM_BYTES;
+  static std::mutex mu;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MGF_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!attr_done[dev]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return MGF_ERR_CUDA;
+      attr_done[dev] = true;
+    }
+  }
+  kern<<<grid, kThreads, smem, st>>>(tA, tB, p);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+template <int BN>
+static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid,
+                        cudaStream_t st) {
+  switch (epi) {
+    case MGF_EPI_BIAS:
+      return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_BIAS, false, false>(tA, tB, p, grid, st);
+    case MGF_EPI_SWIGLU:
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU, false, true>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU, false, false>(tA, tB, p, grid, st);
+    case MGF_EPI_SWIGLU_BWD:
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false>(tA, tB, p, grid, st);
+    case MGF_EPI_WGRAD:
+      return launch_inst<BN, MGF_EPI_WGRAD, true, true>(tA, tB, p, grid, st);
+    default:
+      return MGF_ERR_INVALID_ARGUMENT;
+  }
+}
+
+// N tile: the candidate with the least padding along n, ties to the wider tile.
+static int pick_bn(int64_t n) {
+  const int cands[3] = {256, 192, 128};
+  int best = 256;
+  int64_t best_pad = -1;
+  for (int c : cands) {
+    const int64_t pad = (n + c - 1) / c * c - n;
+    if (best_pad < 0 || pad < best_pad) {
+      best = c;
+      best_pad = pad;
+    }
+  }
+  return best;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace mgf
+
+using namespace mgf;
+
+extern "C" int mgf_version(void) { return 100; }
+
+extern "C" const char* mgf_status_string(int status) {
+  switch (status) {
+    case MGF_OK: return "ok";
+    case MGF_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MGF_ERR_UNSUPPORTED_LAYOUT: return "unsupported layout";
+    case MGF_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+    case MGF_ERR_TOO_MANY_GROUPS: return "number of groups outside 1..1024";
+    case MGF_ERR_CUDA: return "CUDA runtime error";
+    case MGF_ERR_NO_DEVICE_SUPPORT: return "device is not sm_100 (B200)";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int mgf_device_status(int device, uint32_t* status_out, int clear) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return MGF_ERR_CUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return MGF_ERR_CUDA;
+  int rc = MGF_OK;
+  unsigned int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpyFromSymbol(&v, g_status, sizeof(v)) != cudaSuccess) {
+    rc = MGF_ERR_CUDA;
+  } else {
+    if (status_out) *status_out = v;
+    if (clear) {
+      const unsigned int zero = 0;
+      if (cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)) != cudaSuccess) rc = MGF_ERR_CUDA;
+    }
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
+extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) {
+  if (desc == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  const mgf_gemm_desc& g = *desc;
+  if (g.num_groups < 1 || g.num_groups > kMaxGroups) return MGF_ERR_TOO_MANY_GROUPS;
+  if (g.epilogue < MGF_EPI_BIAS || g.epilogue > MGF_EPI_WGRAD) return MGF_ERR_INVALID_ARGUMENT;
+  if (g.offs == nullptr || g.a == nullptr || g.b == nullptr || g.d == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  if (g.total_rows < 0 || g.total_rows > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
+  const bool ragged_k = g.epilogue == MGF_EPI_WGRAD;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MGF_ERR_CUDA;
+  const DeviceInfo di = device_info(dev);
+  if (di.major != 10) return MGF_ERR_NO_DEVICE_SUPPORT;
+
+  Params p{};
+  p.epi = g.epilogue;
+  p.E = g.num_groups;
+  p.total_rows = g.total_rows;
+  p.offs = g.offs;
+  p.bias = static_cast<const __nv_bfloat16*>(g.bias);
+  p.bias_stride = g.bias_stride;
+  p.d = static_cast<__nv_bfloat16*>(g.d);
+  p.ldd = g.ldd;
+  p.ldd_batch = g.ldd_batch;
+  p.d2 = static_cast<__nv_bfloat16*>(g.d2);
+  p.ldd2 = g.ldd2;
+  p.aux = static_cast<const __nv_bfloat16*>(g.aux);
+  p.ld_aux = g.ld_aux;
+  p.alpha = g.swiglu_alpha;
+  p.limit = g.swiglu_limit;
+  p.store_aux = g.store_aux;
+
+  // Every row stride must be a multiple of 8 bf16 (16 bytes) and every base 16-byte aligned:
+  // TMA needs it for A and B, the epilogue's 16-byte vector stores need it for the outputs.
+  auto stride_ok = [](int64_t s) { return s > 0 && (s % 8) == 0; };
+  if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.d)) return MGF_ERR_ALIGNMENT;
+  if (!stride_ok(g.lda) || !stride_ok(g.ldb) || !stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
+
+  CUtensorMap tA, tB;
+  int bn, n_tiles;
+  int64_t tiles_upper;
+  if (!ragged_k) {
+    if (g.n <= 0 || g.k <= 0 || (g.n % 8) != 0 || (g.k % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
+    if (g.n > INT32_MAX || g.k > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
+    if (!stride_ok(g.ldb_batch)) return MGF_ERR_ALIGNMENT;
+    if (g.bias != nullptr && (!aligned16(g.bias) || !stride_ok(g.bias_stride))) return MGF_ERR_ALIGNMENT;
+    if (g.epilogue == MGF_EPI_SWIGLU) {
+      if (g.bias == nullptr || g.d2 == nullptr || (g.n % 16) != 0) return MGF_ERR_INVALID_ARGUMENT;
+      if (!aligned16(g.d2) || !stride_ok(g.ldd2)) return MGF_ERR_ALIGNMENT;
+    }
+    if (g.epilogue == MGF_EPI_SWIGLU_BWD) {
+      if (g.aux == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+      if (!aligned16(g.aux) || !stride_ok(g.ld_aux)) return MGF_ERR_ALIGNMENT;
+    }
+    p.m = 0;
+    p.n = static_cast<int>(g.n);
+    p.k = static_cast<int>(g.k);
+    bn = pick_bn(g.n);
+    n_tiles = static_cast<int>((g.n + bn - 1) / bn);
+    p.n_tiles = n_tiles;
+    if (g.total_rows == 0) return MGF_OK;  // nothing to compute, outputs have no rows
+    const uint64_t dA[2] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.total_rows)};
+    const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
+    const uint32_t bA[2] = {64, 128};
+    if (!encode_bf16(&tA, g.a, 2, dA, sA, bA)) return MGF_ERR_CUDA;
+    const uint64_t sB[2] = {static_cast<uint64_t>(g.ldb) * 2, static_cast<uint64_t>(g.ldb_batch) * 2};
+    if (g.b_mn_major) {
+      const uint64_t dB[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.num_groups)};
+      const uint32_t bB[3] = {64, 64, 1};
+      if (!encode_bf16(&tB, g.b, 3, dB, sB, bB)) return MGF_ERR_CUDA;
+    } else {
+      const uint64_t dB[3] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.num_groups)};
+      const uint32_t bB[3] = {64, static_cast<uint32_t>(bn), 1};
+      if (!encode_bf16(&tB, g.b, 3, dB, sB, bB)) return MGF_ERR_CUDA;
+    }
+    tiles_upper = (g.total_rows / BM + g.num_groups) * static_cast<int64_t>(n_tiles);
+  } else {
+    if (g.m <= 0 || g.n <= 0 || (g.m % 8) != 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
+    if (g.m > INT32_MAX || g.n > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
+    if (!stride_ok(g.ldd_batch)) return MGF_ERR_ALIGNMENT;
+    if (g.d2 != nullptr && (!aligned16(g.d2) || !stride_ok(g.ldd2))) return MGF_ERR_ALIGNMENT;
+    p.m = static_cast<int>(g.m);
+    p.n = static_cast<int>(g.n);
+    p.k = 0;
+    bn = pick_bn(g.n);
+    n_tiles = static_cast<int>((g.n + bn - 1) / bn);
+    p.n_tiles = n_tiles;
+    p.m_tiles_real = static_cast<int>((g.m + BM - 1) / BM);
+    p.bias_grad = g.d2 != nullptr ? 1 : 0;
+    p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % BM) == 0) ? 1 : 0);
+    const uint64_t rows = static_cast<uint64_t>(g.total_rows > 0 ? g.total_rows : 1);
+    const uint64_t dA[2] = {static_cast<uint64_t>(g.m), rows};
+    const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
+    const uint32_t bA[2] = {64, 64};
+    if (!encode_bf16(&tA, g.a, 2, dA, sA, bA)) return MGF_ERR_CUDA;
+    const uint64_t dB[2] = {static_cast<uint64_t>(g.n), rows};
+    const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb) * 2};
+    const uint32_t bB[2] = {64, 64};
+    if (!encode_bf16(&tB, g.b, 2, dB, sB, bB)) return MGF_ERR_CUDA;
+    tiles_upper = static_cast<int64_t>(p.m_tiles) * n_tiles * g.num_groups;
+  }
+
+  int sms = di.sms - (g.sm_carveout > 0 ? g.sm_carveout : 0);
+  if (sms < 1) sms = 1;
+  const int grid = static_cast<int>(tiles_upper < sms ? tiles_upper : sms);
+  if (grid <= 0) return MGF_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool b_mn = ragged_k ? true : (g.b_mn_major != 0);
+  switch (bn) {
+    case 256: return dispatch_epi<256>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    case 192: return dispatch_epi<192>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    default: return dispatch_epi<128>(g.epilogue, b_mn, tA, tB, p, grid, st);
+  }
+}

@@ -1,0 +1,326 @@
+// torch.library registration of the `grouped_mm` operator namespace on top of the C ABI in
+// moe_gemm.h.  Schemas, argument meaning, output allocation (16-byte padded row stride) and the
+// error messages follow Butterfingrz/CuTe-MoE-Train (paths relative to cutlass_op/bf16_grouped_mm/):
+//   grouped_mm::mm            custom_op.py:139-149, csrc/binding.cu:13-34, csrc/cutlass_utils.cuh:26-147
+//   grouped_mm::mm_swiglu     custom_op.py:400-435, csrc/binding.cu:39-64
+//   grouped_mm::mm_swiglu_bwd custom_op.py:534-558, csrc/binding.cu:68-118
+//   grouped_mm::mm_downproj   custom_op.py:579-601
+// Shape inference (fake tensors) and autograd are registered from Python, like the reference.
+// Every launch goes on the current CUDA stream; nothing here synchronises or reads offs on the host.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstring>
+
+#include "moe_gemm.h"
+
+namespace {
+
+using at::Tensor;
+
+void check_launch(int rc, const char* what) {
+  TORCH_CHECK(rc == MGF_OK, what, ": ", mgf_status_string(rc), " (status ", rc, ")");
+}
+
+int64_t padded(int64_t n) { return (n + 7) / 8 * 8; }
+
+// csrc/cutlass_utils.cuh:66-81: one of the last two strides is 1 and the other a multiple of
+// 16 bytes; returns true when the matrix is column-major (stride(-2) == 1).
+bool check_strides_transposed(const Tensor& mat, const char* name) {
+  const auto st = mat.strides();
+  const auto sz = mat.sizes();
+  const int end = mat.dim() - 1;
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(mat.data_ptr()) % 16 == 0, name,
+              ": expected data_ptr to be aligned to 16 bytes");
+  if (st[end - 1] == 1 && st[end] >= std::max<int64_t>(1, sz[end - 1])) {
+    TORCH_CHECK(st[end] % 8 == 0, name, ": strides should be multiple of 16 bytes");
+    return true;
+  }
+  if (st[end] == 1 && st[end - 1] >= std::max<int64_t>(1, sz[end])) {
+    TORCH_CHECK(st[end - 1] % 8 == 0, name, ": strides should be multiple of 16 bytes");
+    return false;
+  }
+  TORCH_CHECK(false, "Invalid strides/sizes, got ", mat.strides(), " for strides and ", mat.sizes(), " for sizes");
+  return false;
+}
+
+void check_offs(const Tensor& offs, const Tensor& ref) {
+  TORCH_CHECK(offs.dim() == 1, "offs has to be 1D");
+  TORCH_CHECK(offs.scalar_type() == at::kInt, "Offsets have to be int32");
+  TORCH_CHECK(offs.is_contiguous(), "offs must be contiguous");
+  TORCH_CHECK(offs.device() == ref.device(), "All tensors must be on the same device");
+  TORCH_CHECK(offs.numel() >= 1 && offs.numel() <= 1024, "group count must be in [1, 1024], got ", offs.numel());
+}
+
+void check_bias(const Tensor& bias, int64_t groups, int64_t n) {
+  TORCH_CHECK(bias.scalar_type() == at::kBFloat16, "Bias must be BFloat16, got ", bias.scalar_type());
+  TORCH_CHECK(bias.dim() == 2, "Bias must be 2D [group_count, N] for per-group bias, got ", bias.dim(), "D");
+  TORCH_CHECK(bias.size(0) == groups, "Bias first dimension must match group_count, expected ", groups, " got ",
+              bias.size(0));
+  TORCH_CHECK(bias.size(1) == n, "Bias second dimension must match N dimension, expected ", n, " got ", bias.size(1));
+  TORCH_CHECK(bias.is_contiguous(), "Bias must be contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(bias.data_ptr()) % 16 == 0,
+              "Bias data pointer must be 16-byte aligned for TMA transfers");
+  TORCH_CHECK(bias.size(1) % 8 == 0, "Bias N dimension must be multiple of 8 elements (16 bytes), got ",
+              bias.size(1));
+}
+
+mgf_gemm_desc base_desc() {
+  mgf_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.swiglu_alpha = 1.702f;
+  d.swiglu_limit = 7.0f;
+  d.sm_carveout = 0;
+  return d;
+}
+
+int sm_carveout_for(const Tensor& t) {
+  // Honour PyTorch's SM carve-out knob (the reference reads it at
+  // csrc/grouped_mm_kernel.cuh:355-356) so collectives can keep SMs free.
+  auto c = at::globalContext()._SMCarveout_EXPERIMENTAL();
+  (void)t;
+  return c.has_value() ? static_cast<int>(*c) : 0;
+}
+
+// Ragged-M launch: A [total_rows, k] row-major, B [E, k, n] (either major), D [total_rows, n].
+void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& offs, const Tensor* bias,
+                     const Tensor& d, const Tensor* d2, const Tensor* aux, double alpha, double limit,
+                     bool store_aux, const char* what) {
+  const bool b_col_major = check_strides_transposed(b, "mat_b");
+  mgf_gemm_desc g = base_desc();
+  g.epilogue = epi;
+  g.num_groups = static_cast<int32_t>(offs.numel());
+  g.total_rows = a.size(0);
+  g.k = a.size(1);
+  g.n = b.size(2);
+  g.a = a.data_ptr();
+  g.lda = a.stride(0);
+  g.b = b.data_ptr();
+  g.b_mn_major = b_col_major ? 0 : 1;
+  g.ldb = b_col_major ? b.stride(2) : b.stride(1);
+  g.ldb_batch = b.stride(0);
+  g.offs = offs.data_ptr<int32_t>();
+  if (bias != nullptr) {
+    g.bias = bias->data_ptr();
+    g.bias_stride = bias->stride(0);
+  }
+  g.d = d.data_ptr();
+  g.ldd = d.stride(0);
+  if (d2 != nullptr) {
+    g.d2 = d2->data_ptr();
+    g.ldd2 = d2->stride(0);
+  }
+  if (aux != nullptr) {
+    g.aux = aux->data_ptr();
+    g.ld_aux = aux->stride(0);
+  }
+  g.swiglu_alpha = static_cast<float>(alpha);
+  g.swiglu_limit = static_cast<float>(limit);
+  g.store_aux = store_aux ? 1 : 0;
+  g.sm_carveout = sm_carveout_for(a);
+  check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
+}
+
+// Ragged-K launch: mat_a [M, total_K] is the transposed view (stride(0) == 1) of a row-major
+// [total_K, M] matrix, mat_b [total_K, N] is row-major; returns (D [E, M, N], db [E, N] or undefined).
+std::tuple<Tensor, Tensor> ragged_k_launch(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                           bool bias_grad, const char* what) {
+  TORCH_CHECK(mat_a.stride(0) == 1, what,
+              ": ragged-K needs mat_a as a transposed row-major matrix (stride(0) == 1)");
+  TORCH_CHECK(mat_b.stride(1) == 1, what, ": ragged-K needs a row-major mat_b");
+  TORCH_CHECK(mat_a.size(1) == mat_b.size(0), "contraction dimension of mat_a and mat_b must match");
+  const int64_t E = offs.size(0), M = mat_a.size(0), N = mat_b.size(1);
+  Tensor out = at::empty_strided({E, M, N}, {M * padded(N), padded(N), 1}, mat_a.options());
+  Tensor db;
+  mgf_gemm_desc g = base_desc();
+  g.epilogue = MGF_EPI_WGRAD;
+  g.num_groups = static_cast<int32_t>(E);
+  g.total_rows = mat_a.size(1);
+  g.m = M;
+  g.n = N;
+  g.a = mat_a.data_ptr();
+  g.lda = mat_a.stride(1);
+  g.b = mat_b.data_ptr();
+  g.ldb = mat_b.stride(0);
+  g.offs = offs.data_ptr<int32_t>();
+  g.d = out.data_ptr();
+  g.ldd = out.stride(1);
+  g.ldd_batch = out.stride(0);
+  if (bias_grad) {
+    db = at::empty({E, N}, mat_a.options());
+    g.d2 = db.data_ptr();
+    g.ldd2 = db.stride(0);
+  }
+  g.sm_carveout = sm_carveout_for(mat_a);
+  check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
+  return {out, db};
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm
+Tensor mm_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::optional<Tensor>& offs,
+               const std::optional<Tensor>& bias, int64_t out_dtype) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm: inputs must be CUDA tensors");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  TORCH_CHECK(mat_a.dim() == 2 || mat_a.dim() == 3, "mat_a has to be 2 or 3d");
+  TORCH_CHECK(mat_b.dim() == 2 || mat_b.dim() == 3, "mat_b has to be 2 or 3d");
+  const bool a2 = mat_a.dim() == 2, b2 = mat_b.dim() == 2;
+  if (!a2 || !b2)
+    TORCH_CHECK(mat_a.size(-1) == mat_b.size(-2), "contraction dimension of mat_a and mat_b must match");
+  TORCH_CHECK(offs.has_value() == (a2 || b2),
+              "Have to provide offsets if there is a 2d matrix, or no offset if both matrices are 3d");
+  if (out_dtype != -1)
+    TORCH_CHECK(static_cast<c10::ScalarType>(out_dtype) == mat_a.scalar_type(),
+                "Grouped gemm output dtype must match `mat_a` dtype");
+  TORCH_CHECK(mat_a.scalar_type() == at::kBFloat16 && mat_b.scalar_type() == at::kBFloat16,
+              "grouped_mm CUDA kernel currently supports only BFloat16 inputs/output. Got mat_a=",
+              mat_a.scalar_type(), ", mat_b=", mat_b.scalar_type());
+  const bool a_col = check_strides_transposed(mat_a, "mat_a");
+  check_strides_transposed(mat_b, "mat_b");
+  if (offs.has_value()) check_offs(*offs, mat_a);
+
+  if (a2 && !b2) {
+    // ragged-M: out [total_M, N]
+    TORCH_CHECK(offs->size(0) == mat_b.size(0), "matrix batch sizes have to match");
+    TORCH_CHECK(!a_col, "grouped_mm: ragged-M with a column-major mat_a is not supported on this path");
+    const int64_t N = mat_b.size(2);
+    if (bias.has_value()) check_bias(*bias, mat_b.size(0), N);
+    Tensor out = at::empty_strided({mat_a.size(0), N}, {padded(N), 1}, mat_a.options());
+    launch_ragged_m(MGF_EPI_BIAS, mat_a, mat_b, *offs, bias.has_value() ? &*bias : nullptr, out, nullptr, nullptr,
+                    1.702, 7.0, false, "grouped_mm");
+    return out;
+  }
+  if (a2 && b2) {
+    TORCH_CHECK(!bias.has_value(), "grouped_mm: bias is not supported on the ragged-K path");
+    return std::get<0>(ragged_k_launch(mat_a, mat_b, *offs, false, "grouped_mm"));
+  }
+  if (!a2 && !b2) {
+    // batched: [B, M, K] x [B, K, N] -> [B, M, N]; run as ragged-M with equal groups.
+    TORCH_CHECK(mat_a.size(0) == mat_b.size(0), "batched dimension has to match");
+    TORCH_CHECK(!a_col && mat_a.stride(0) == mat_a.size(1) * mat_a.stride(1),
+                "grouped_mm: batched mat_a must be row-major with packed batches on this path");
+    const int64_t B = mat_a.size(0), M = mat_a.size(1), N = mat_b.size(2);
+    if (bias.has_value()) check_bias(*bias, B, N);
+    Tensor out = at::empty_strided({B, M, N}, {M * padded(N), padded(N), 1}, mat_a.options());
+    TORCH_CHECK(B >= 1 && B <= 1024, "group count must be in [1, 1024]");
+    Tensor boffs = at::arange(1, B + 1, mat_a.options().dtype(at::kInt)).mul_(static_cast<int>(M));
+    Tensor a_flat = mat_a.reshape({B * M, mat_a.size(2)});
+    Tensor out_flat = out.view({B * M, padded(N)}).narrow(1, 0, N);
+    launch_ragged_m(MGF_EPI_BIAS, a_flat, mat_b, boffs, bias.has_value() ? &*bias : nullptr, out_flat, nullptr,
+                    nullptr, 1.702, 7.0, false, "grouped_mm");
+    return out;
+  }
+  TORCH_CHECK(false, "grouped_mm: ragged-N (3D x 2D) is not supported on this path");
+  return Tensor();
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm_swiglu
+std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                          const Tensor& bias, double alpha, double limit) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm_swiglu: inputs must be CUDA tensors");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 3, "grouped_mm_swiglu requires mat_a 2D and mat_b 3D (ragged-M path)");
+  TORCH_CHECK(mat_a.scalar_type() == at::kBFloat16 && mat_b.scalar_type() == at::kBFloat16,
+              "grouped_mm_swiglu requires BFloat16 inputs");
+  TORCH_CHECK(bias.scalar_type() == at::kBFloat16, "bias must be BFloat16");
+  TORCH_CHECK(offs.scalar_type() == at::kInt, "offs must be int32");
+  TORCH_CHECK(mat_a.size(1) == mat_b.size(1), "contraction dimension of mat_a and mat_b must match");
+  TORCH_CHECK(!check_strides_transposed(mat_a, "mat_a"), "grouped_mm_swiglu requires a row-major mat_a");
+  check_offs(offs, mat_a);
+  TORCH_CHECK(offs.size(0) == mat_b.size(0), "matrix batch sizes have to match");
+  const int64_t N = mat_b.size(2);
+  TORCH_CHECK(N % 16 == 0, "grouped_mm_swiglu: 2*I must be a multiple of 16, got ", N);
+  check_bias(bias, mat_b.size(0), N);
+  const int64_t M = mat_a.size(0);
+  Tensor swiglu_out = at::empty_strided({M, N / 2}, {padded(N / 2), 1}, mat_a.options());
+  Tensor aux_out = at::empty_strided({M, N}, {padded(N), 1}, mat_a.options());
+  launch_ragged_m(MGF_EPI_SWIGLU, mat_a, mat_b, offs, &bias, aux_out, &swiglu_out, nullptr, alpha, limit, true,
+                  "grouped_mm_swiglu");
+  return {swiglu_out, aux_out};
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm_swiglu_bwd
+Tensor mm_swiglu_bwd_cuda(const Tensor& grad_out_in, const Tensor& down_w_t, const Tensor& offs,
+                          const Tensor& aux_biased_acc, double alpha, double limit) {
+  TORCH_CHECK(grad_out_in.is_cuda(), "grouped_mm_swiglu_bwd: inputs must be CUDA tensors");
+  const c10::cuda::CUDAGuard guard(grad_out_in.device());
+  if (grad_out_in.numel() == 0) return at::zeros_like(aux_biased_acc);
+  Tensor grad_out = grad_out_in.contiguous();
+  TORCH_CHECK(grad_out.dim() == 2, "grad_output must be 2D [M, H]");
+  TORCH_CHECK(down_w_t.dim() == 3, "down_w_t must be 3D [E, H, I]");
+  TORCH_CHECK(aux_biased_acc.dim() == 2, "aux_biased_acc must be 2D [M, 2*I]");
+  TORCH_CHECK(grad_out.scalar_type() == at::kBFloat16 && down_w_t.scalar_type() == at::kBFloat16,
+              "_grouped_mm_swiglu_bwd_cuda requires bf16 grad_output and down_w_t");
+  TORCH_CHECK(aux_biased_acc.scalar_type() == at::kBFloat16, "aux_biased_acc must be bfloat16, got ",
+              aux_biased_acc.scalar_type());
+  TORCH_CHECK(aux_biased_acc.size(-1) % 2 == 0, "aux_biased_acc.shape[-1] must be even for bf16 pair packing");
+  TORCH_CHECK(aux_biased_acc.stride(-1) == 1, "aux_biased_acc must have stride(-1) == 1 for packed view");
+  TORCH_CHECK(aux_biased_acc.stride(-2) % 2 == 0, "aux_biased_acc.stride(-2) must be even for packed fp32 reinterpretation");
+  check_offs(offs, grad_out);
+  TORCH_CHECK(grad_out.size(0) == aux_biased_acc.size(0), "Expected [M, I] packed tensors with matching shape");
+  TORCH_CHECK(down_w_t.size(0) == offs.size(0), "down_w_t.shape[0] must match offs.size(0)");
+  TORCH_CHECK(grad_out.size(1) == down_w_t.size(1), "grad_output.shape[1] must match down_w_t.shape[1] (H)");
+  TORCH_CHECK(down_w_t.size(2) * 2 == aux_biased_acc.size(1), "down_w_t.shape[2] must match aux_packed.shape[1] (I)");
+  TORCH_CHECK(grad_out.device() == down_w_t.device() && down_w_t.device() == aux_biased_acc.device(),
+              "All tensors must be on the same device");
+  Tensor grad_aux = at::empty_like(aux_biased_acc, at::MemoryFormat::Contiguous);
+  TORCH_CHECK(grad_aux.stride(0) == aux_biased_acc.size(1), "grad_aux layout");
+  launch_ragged_m(MGF_EPI_SWIGLU_BWD, grad_out, down_w_t, offs, nullptr, grad_aux, nullptr, &aux_biased_acc, alpha,
+                  limit, false, "grouped_mm_swiglu_bwd");
+  return grad_aux;
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm_downproj
+Tensor mm_downproj_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::optional<Tensor>& offs,
+                        const std::optional<Tensor>& bias, const Tensor& /*aux_biased_acc*/, double /*alpha*/,
+                        double /*limit*/) {
+  TORCH_CHECK(offs.has_value(), "grouped_mm::mm_downproj requires offs for ragged-M path");
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 3, "grouped_mm::mm_downproj requires mat_a 2D and mat_b 3D");
+  return mm_cuda(mat_a, mat_b, offs, bias, -1);
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm_wgrad_bias
+// Weight gradient of a ragged-M layer fused with its bias gradient: for every group e,
+// dW[e] = mat_a[:, rows(e)] @ mat_b[rows(e), :] and db[e] = sum over rows(e) of mat_b (fp32
+// accumulation, one bf16 rounding).  Replaces the separate `_segment_sum_rows` pass of the
+// reference (custom_op.py:79-101, called at custom_op.py:516-518 and 666-667).
+std::tuple<Tensor, Tensor> mm_wgrad_bias_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm_wgrad_bias: inputs must be CUDA tensors");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 2, "grouped_mm_wgrad_bias requires 2D mat_a and mat_b");
+  TORCH_CHECK(mat_a.scalar_type() == at::kBFloat16 && mat_b.scalar_type() == at::kBFloat16,
+              "grouped_mm_wgrad_bias requires BFloat16 inputs");
+  check_strides_transposed(mat_a, "mat_a");
+  check_strides_transposed(mat_b, "mat_b");
+  check_offs(offs, mat_a);
+  return ragged_k_launch(mat_a, mat_b, offs, true, "grouped_mm_wgrad_bias");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(grouped_mm, m) {
+  m.def("mm(Tensor mat_a, Tensor mat_b, Tensor? offs, Tensor? bias, int out_dtype) -> Tensor");
+  m.def(
+      "mm_swiglu(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha, float swiglu_limit)"
+      " -> (Tensor, Tensor)");
+  m.def(
+      "mm_swiglu_bwd(Tensor grad_out, Tensor down_w_t, Tensor offs, Tensor aux_biased_acc, float swiglu_alpha,"
+      " float swiglu_limit) -> Tensor");
+  m.def(
+      "mm_downproj(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor aux_biased_acc,"
+      " float swiglu_alpha, float swiglu_limit) -> Tensor");
+  m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
+  m.impl("mm", &mm_cuda);
+  m.impl("mm_swiglu", &mm_swiglu_cuda);
+  m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
+  m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
+  m.impl("mm_downproj",
+         [](const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
+            const Tensor& aux, double alpha, double limit) {
+           return mm_downproj_cuda(a, b, offs, bias, aux, alpha, limit);
+         });
+}

@@ -1,0 +1,65 @@
+"""Loader for the native libraries of the MoE FFN grouped-GEMM path.
+
+`libmoe_gemm.so` holds the sm_100a kernels behind the C ABI of include/moe_gemm.h;
+`_grouped_mm_ops.so` registers the `grouped_mm::*` torch operators on top of it.  Both are built
+in-tree by cute-moe-train_b200/build.py.  There is no fallback: if a library is missing the
+import fails with the command that builds it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libmoe_gemm.so"
+OPS_PATH = _HERE / "_grouped_mm_ops.so"
+
+# Device status bits (include/moe_gemm.h).
+DEV_WAIT_TIMEOUT = 0x1
+DEV_BAD_OFFS = 0x2
+
+
+def _require(path: Path) -> None:
+    if not path.exists():
+        raise ImportError(
+            f"{path.name} is not built; run `python cute-moe-train_b200/build.py` "
+            "(or __graft_entry__.build()) first. This path has no CPU fallback."
+        )
+
+
+_require(LIB_PATH)
+_require(OPS_PATH)
+# Load the C-ABI library first (global symbols) so the ops library resolves against this copy.
+lib = ctypes.CDLL(str(LIB_PATH), mode=ctypes.RTLD_GLOBAL)
+lib.mgf_version.restype = ctypes.c_int
+lib.mgf_status_string.restype = ctypes.c_char_p
+lib.mgf_status_string.argtypes = [ctypes.c_int]
+lib.mgf_device_status.restype = ctypes.c_int
+lib.mgf_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
+torch.ops.load_library(str(OPS_PATH))
+
+
+def device_status(device: int | None = None, clear: bool = True) -> int:
+    """Synchronise `device` and return its kernel status bits (0 = clean); clears them by default."""
+    if device is None:
+        device = torch.cuda.current_device()
+    out = ctypes.c_uint32(0)
+    rc = lib.mgf_device_status(int(device), ctypes.byref(out), 1 if clear else 0)
+    if rc != 0:
+        raise RuntimeError(f"mgf_device_status failed: {lib.mgf_status_string(rc).decode()}")
+    return int(out.value)
+
+
+def check_device_status(device: int | None = None) -> None:
+    """Raise RuntimeError if a kernel on `device` recorded a problem since the last check."""
+    st = device_status(device, clear=True)
+    if st:
+        what = []
+        if st & DEV_WAIT_TIMEOUT:
+            what.append("a pipeline wait ran out and the kernel stopped early")
+        if st & DEV_BAD_OFFS:
+            what.append("offs was not non-decreasing within [0, total rows]")
+        raise RuntimeError("grouped_mm device status: " + "; ".join(what))

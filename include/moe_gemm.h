@@ -1,0 +1,122 @@
+/*
+ * moe_gemm.h -- C ABI of the B200 (sm_100a) MoE FFN grouped-GEMM library (libmoe_gemm.so).
+ *
+ * One launcher runs every GEMM of the MoE FFN forward and backward.  A call describes one
+ * grouped GEMM over E experts whose token rows are delimited by `offs` (int32 cumulative
+ * end offsets, on the device) and picks one of four fused epilogues.  All pointers are
+ * device pointers; nothing here allocates, synchronises the host or reads `offs` on the host.
+ *
+ * Reference interfaces this ABI replaces (Butterfingrz/CuTe-MoE-Train,
+ * paths relative to cutlass_op/bf16_grouped_mm/):
+ *   MGF_EPI_BIAS            <- csrc/binding.cu:13-34  `_grouped_mm_cuda` (ragged-M, bias optional)
+ *                              and csrc/grouped_mm_kernel.cuh:478 `bf16bf16_grouped_mm`
+ *   MGF_EPI_SWIGLU          <- csrc/binding.cu:39-64  `_grouped_mm_swiglu_cuda`
+ *                              and csrc/grouped_mm_kernel.cuh:1365 `bf16bf16_grouped_mm_swiglu`
+ *   MGF_EPI_SWIGLU_BWD      <- csrc/binding.cu:68-118 `_grouped_mm_swiglu_bwd_cuda`
+ *                              and csrc/grouped_mm_kernel.cuh:854 `bf16bf16_grouped_mm_swiglu_bwd`
+ *   MGF_EPI_WGRAD           <- the ragged-K (2D x 2D) branch of `_grouped_mm_cuda`
+ *                              (csrc/grouped_mm_kernel.cuh:224-226, csrc/grouped_mm_common.cuh:120-133)
+ *                              fused with custom_op.py:79-101 `_segment_sum_rows` (bias gradient)
+ *
+ * Error behaviour: host-side argument errors return a negative MGF_ERR_* code and launch
+ * nothing (the torch layer turns them into RuntimeError, like the reference's TORCH_CHECKs).
+ * Device-side problems (malformed offs, a pipeline wait that ran out) never trap: the kernel
+ * records a bit in a device status word that mgf_device_status() reads.
+ */
+#ifndef MOE_GEMM_H_
+#define MOE_GEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Epilogue selector. */
+enum mgf_epilogue {
+  MGF_EPI_BIAS = 0,       /* D = bf16(A*B[e] + bias[e])           (bias may be NULL)          */
+  MGF_EPI_SWIGLU = 1,     /* aux = bf16(A*B[e] + bias[e]); D2 = swiglu(aux) (gate/up interleaved) */
+  MGF_EPI_SWIGLU_BWD = 2, /* D = swiglu_bwd(A*B[e], aux): interleaved (d_gate, d_up) pairs     */
+  MGF_EPI_WGRAD = 3       /* ragged-K: D[e] = A[g]^T-view * B[g]; D2[e] = column sums of B[g]  */
+};
+
+/* Status codes returned by the host entry points. */
+enum mgf_status {
+  MGF_OK = 0,
+  MGF_ERR_INVALID_ARGUMENT = -1,
+  MGF_ERR_UNSUPPORTED_LAYOUT = -2,
+  MGF_ERR_ALIGNMENT = -3,
+  MGF_ERR_TOO_MANY_GROUPS = -4,
+  MGF_ERR_CUDA = -5,
+  MGF_ERR_NO_DEVICE_SUPPORT = -6
+};
+
+/* Device status bits recorded by the kernels (read with mgf_device_status). */
+#define MGF_DEV_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out; the kernel stopped early        */
+#define MGF_DEV_BAD_OFFS 0x2u      /* offs not non-decreasing or beyond the row extent; clamped */
+
+/*
+ * One grouped GEMM.  Matrix layouts are given as element strides of bf16 tensors.
+ *
+ * Ragged-M epilogues (BIAS, SWIGLU, SWIGLU_BWD):
+ *   A    : [total_rows, k] row-major (stride lda, unit stride along k); rows of group e are
+ *          offs[e-1]..offs[e]-1.
+ *   B    : [E, k, n] with batch stride ldb_batch; b_mn_major=1 means unit stride along n
+ *          (row stride ldb), b_mn_major=0 means unit stride along k (column stride ldb).
+ *   D    : [total_rows, n_out] row-major, stride ldd (n_out = n, or the aux tensor for SWIGLU).
+ *   D2   : SWIGLU only: swiglu_out [total_rows, n/2], stride ldd2.
+ *   aux  : SWIGLU_BWD only: [total_rows, 2n] interleaved (gate, up), stride ld_aux; D is then
+ *          grad_aux [total_rows, 2n] with stride ldd.
+ * Ragged-K epilogue (WGRAD):
+ *   A    : [total_rows, m] row-major (stride lda): the GEMM uses its transpose per group.
+ *   B    : [total_rows, n] row-major (stride ldb).
+ *   D    : [E, m, n] bf16, row stride ldd, batch stride ldd_batch.  Empty groups get zeros.
+ *   D2   : optional [E, n] bf16 bias gradient (stride ldd2 between groups): column sums of B.
+ */
+typedef struct mgf_gemm_desc {
+  int32_t epilogue;      /* enum mgf_epilogue */
+  int32_t num_groups;    /* E (1..1024) */
+  int64_t total_rows;    /* extent of the ragged dimension (tokens) */
+  int64_t m, n, k;       /* fixed GEMM extents (m unused for ragged-M, k unused for ragged-K) */
+  const void* a;
+  int64_t lda;
+  const void* b;
+  int64_t ldb;
+  int64_t ldb_batch;
+  int32_t b_mn_major;
+  const int32_t* offs;   /* device int32 [E] cumulative end offsets */
+  const void* bias;      /* device bf16 [E, n] or NULL */
+  int64_t bias_stride;
+  void* d;
+  int64_t ldd;
+  int64_t ldd_batch;
+  void* d2;
+  int64_t ldd2;
+  const void* aux;
+  int64_t ld_aux;
+  float swiglu_alpha;
+  float swiglu_limit;
+  int32_t store_aux;     /* SWIGLU: 1 = also write aux (D) */
+  int32_t sm_carveout;   /* SMs left free for concurrent work (collectives); 0 = use all */
+} mgf_gemm_desc;
+
+/* Launch one grouped GEMM on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Replaces: csrc/binding.cu:13-148 (the three pybind entry points) + the dispatch in
+ * csrc/grouped_mm_kernel.cuh:390-486, 760-864, 1267-1390. */
+int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream);
+
+/* Read (and optionally clear) the device status word of `device`.  Synchronises that
+ * device; meant for tests and debugging, never called on the hot path. */
+int mgf_device_status(int device, uint32_t* status_out, int clear);
+
+/* Human-readable text for a mgf_status code. */
+const char* mgf_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+int mgf_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_GEMM_H_ */

@@ -1,0 +1,42 @@
+"""The C-ABI library loads and exports every entry point include/moe_gemm.h declares; host-side
+argument checks answer without a GPU."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "moe_gemm.h"
+LIB = REPO / "cute-moe-train_b200" / "cutlass_op" / "bf16_grouped_mm" / "libmoe_gemm.so"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(mgf_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "mgf_grouped_gemm_launch" in names and "mgf_device_status" in names
+    assert len(names) >= 4
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(LIB))
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} not exported by {LIB.name}"
+
+
+def test_status_strings_and_version():
+    lib = ctypes.CDLL(str(LIB))
+    lib.mgf_status_string.restype = ctypes.c_char_p
+    assert lib.mgf_version() >= 100
+    assert lib.mgf_status_string(0) == b"ok"
+    assert b"alignment" in lib.mgf_status_string(-3) or b"aligned" in lib.mgf_status_string(-3)
+
+
+def test_null_descriptor_rejected():
+    lib = ctypes.CDLL(str(LIB))
+    assert lib.mgf_grouped_gemm_launch(None, None) == -1

@@ -1,0 +1,103 @@
+"""Operator schemas, wrapper signatures and fake-tensor shape inference (no GPU needed)."""
+
+from __future__ import annotations
+
+import inspect
+
+import pytest
+import torch
+
+
+def _pkg():
+    import cutlass_op.bf16_grouped_mm as m
+
+    return m
+
+
+REF_SCHEMAS = {
+    "mm": "grouped_mm::mm(Tensor mat_a, Tensor mat_b, Tensor? offs, Tensor? bias, int out_dtype) -> Tensor",
+    "mm_swiglu": "grouped_mm::mm_swiglu(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha, "
+                 "float swiglu_limit) -> (Tensor, Tensor)",
+    "mm_swiglu_bwd": "grouped_mm::mm_swiglu_bwd(Tensor grad_out, Tensor down_w_t, Tensor offs, Tensor aux_biased_acc, "
+                     "float swiglu_alpha, float swiglu_limit) -> Tensor",
+    "mm_downproj": "grouped_mm::mm_downproj(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, "
+                   "Tensor aux_biased_acc, float swiglu_alpha, float swiglu_limit) -> Tensor",
+}
+
+
+@pytest.mark.parametrize("op", sorted(REF_SCHEMAS))
+def test_schema_matches_reference(op):
+    _pkg()
+    schema = str(getattr(torch.ops.grouped_mm, op).default._schema)
+    assert schema == REF_SCHEMAS[op]
+
+
+def test_wrapper_signatures_and_defaults():
+    m = _pkg()
+    s = inspect.signature(m.grouped_mm_swiglu)
+    assert list(s.parameters) == ["mat_a", "mat_b", "offs", "bias", "swiglu_alpha", "swiglu_limit"]
+    assert s.parameters["swiglu_alpha"].default == 1.702 and s.parameters["swiglu_limit"].default == 7.0
+    s = inspect.signature(m.grouped_mm_downproj)
+    assert list(s.parameters) == ["mat_a", "mat_b", "offs", "bias", "aux_biased_acc", "swiglu_alpha", "swiglu_limit"]
+    s = inspect.signature(m.grouped_mm)
+    assert list(s.parameters) == ["mat_a", "mat_b", "offs", "bias", "out_dtype"]
+    assert set(m.__all__) == {"grouped_mm", "grouped_mm_downproj", "grouped_mm_swiglu"}
+
+
+def _meta(*shape, dtype=torch.bfloat16):
+    return torch.empty(*shape, dtype=dtype, device="meta")
+
+
+def test_fake_shapes_ffn():
+    m = _pkg()
+    E, H, I, M = 8, 2048, 1024, 864
+    x, wu, bu = _meta(M, H), _meta(E, H, 2 * I), _meta(E, 2 * I)
+    wd, bd = _meta(E, I, H), _meta(E, H)
+    offs = _meta(E, dtype=torch.int32)
+    s, aux = m.grouped_mm_swiglu(x, wu, offs, bu)
+    assert s.shape == (M, I) and aux.shape == (M, 2 * I) and s.stride() == (I, 1)
+    out = m.grouped_mm_downproj(s, wd, offs, bd, aux)
+    assert out.shape == (M, H)
+    g = torch.ops.grouped_mm.mm_swiglu_bwd(out, wd.transpose(-2, -1), offs, aux, 1.702, 7.0)
+    assert g.shape == aux.shape
+    dw, db = torch.ops.grouped_mm.mm_wgrad_bias(x.transpose(0, 1), aux, offs)
+    assert dw.shape == (E, H, 2 * I) and db.shape == (E, 2 * I)
+
+
+def test_fake_shapes_grouped_mm_variants():
+    m = _pkg()
+    offs = _meta(4, dtype=torch.int32)
+    assert m.grouped_mm(_meta(100, 64), _meta(4, 64, 40), offs).shape == (100, 40)
+    # padded row stride for N not a multiple of 8 (16-byte rule)
+    assert m.grouped_mm(_meta(100, 64), _meta(4, 64, 36), offs).stride() == (40, 1)
+    assert m.grouped_mm(_meta(64, 100), _meta(100, 40), offs).shape == (4, 64, 40)
+    assert m.grouped_mm(_meta(3, 10, 64), _meta(3, 64, 40)).shape == (3, 10, 40)
+
+
+def test_out_dtype_codes():
+    from cutlass_op.bf16_grouped_mm.custom_op import _dtype_from_int, dtype_to_int
+
+    assert dtype_to_int(None) == -1
+    assert _dtype_from_int(dtype_to_int(torch.bfloat16)) == torch.bfloat16
+
+
+def test_cpu_tensors_rejected_loudly():
+    """No CPU fallback: CPU inputs raise instead of computing."""
+    m = _pkg()
+    x = torch.zeros(8, 16, dtype=torch.bfloat16)
+    w = torch.zeros(1, 16, 32, dtype=torch.bfloat16)
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        m.grouped_mm_swiglu(x, w, torch.tensor([8], dtype=torch.int32), torch.zeros(1, 32, dtype=torch.bfloat16))
+
+
+def test_zipf_routing_properties():
+    from cutlass_op.bf16_grouped_mm.workloads import offs_from_counts, zipf_routing
+
+    c = zipf_routing(24576, 32, 4, 1.1, seed=0, zero_experts=2)
+    assert int(c.sum()) == 24576 * 4
+    assert int((c == 0).sum()) >= 2
+    assert int(c.max()) <= 24576  # without replacement: at most one copy of a token per expert
+    assert any(int(v) % 128 for v in c)
+    offs = offs_from_counts(c)
+    assert offs.dtype == torch.int32 and int(offs[-1]) == 24576 * 4
+    assert torch.equal(zipf_routing(24576, 32, 4, 1.1, seed=0, zero_experts=2), c)

@@ -1,0 +1,76 @@
+"""The CPU oracle against the golden vectors produced by the reference's own Python layer."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import moe_ffn as O
+
+CASES = ["mixed_empty", "odd_sizes", "single_expert", "leading_trailing_empty", "all_empty"]
+KEYS = ["swiglu_out", "aux", "out", "dx", "dw_up", "db_up", "dw_down", "db_down"]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_kernel_chain_matches_reference_layer(golden, case):
+    c = golden["cases"][case]
+    i = c["inputs"]
+    got = O.kernel_chain(i["x"], i["w_up"], i["b_up"], i["w_down"], i["b_down"], i["offs"], i["grad_out"])
+    for k in KEYS:
+        r = O.check(k, got[k], c["outputs"][k].float())
+        assert r["ok"], f"{case}/{k}: rel={r['rel']:.3e} cos={r['cos']:.7f}"
+    # aux is GEMM + bias with a single bf16 rounding in both: exact
+    assert torch.equal(got["aux"].to(torch.bfloat16), c["outputs"]["aux"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fp32_composition_matches_reference_layer(golden, case):
+    c = golden["cases"][case]
+    i = c["inputs"]
+    got = O.fp32_composition(i["x"], i["w_up"], i["b_up"], i["w_down"], i["b_down"], i["offs"], i["grad_out"])
+    rows = int(i["offs"][-1])
+    for k in ["out", "dx", "dw_up", "db_up", "dw_down", "db_down"]:
+        ref = c["outputs"][k].float()
+        g = got[k]
+        if k in ("out", "dx"):
+            g, ref = g[:rows], ref[:rows]
+        r = O.check(k, g, ref)
+        assert r["ok"], f"{case}/{k}: rel={r['rel']:.3e} cos={r['cos']:.7f}"
+
+
+def test_golden_inputs_match_workload_generator(golden):
+    """The fixtures' inputs are exactly what workloads.small_case draws for the same seed."""
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    for name, c in golden["cases"].items():
+        got = small_case(c["E"], c["H"], c["I"], c["counts"], c["seed"], grad=c["grad"])
+        for k, v in zip(["x", "w_up", "b_up", "w_down", "b_down", "offs", "grad_out"], got):
+            assert torch.equal(v, c["inputs"][k]), f"{name}/{k}"
+
+
+def test_empty_groups_give_exact_zero_weight_grads(golden):
+    for name, c in golden["cases"].items():
+        for e, n in enumerate(c["counts"]):
+            if n == 0:
+                for k in ("dw_up", "db_up", "dw_down", "db_down"):
+                    assert torch.count_nonzero(c["outputs"][k][e]) == 0, f"{name}/{k}[{e}]"
+
+
+def test_swiglu_clamp_semantics():
+    """min() on gate only, two-sided clamp on up, inclusive masks in backward."""
+    aux = torch.tensor([[8.0, 8.0, -9.0, -9.0, 7.0, -7.0]])
+    y = O.swiglu_fwd(aux)
+    g = torch.tensor([7.0, -9.0, 7.0])
+    u = torch.tensor([7.0, -7.0, -7.0])
+    ref = g * torch.sigmoid(1.702 * g) * (u + 1)
+    assert torch.allclose(y[0], ref)
+    d = O.swiglu_bwd(torch.ones(1, 3), aux)
+    assert d[0, 0] == 0.0 and d[0, 1] == 0.0  # gate 8 > limit, up 8 > limit
+    assert d[0, 2] != 0.0 and d[0, 3] == 0.0  # gate -9 passes min(), up -9 < -limit
+    assert d[0, 4] != 0.0 and d[0, 5] != 0.0  # exactly at the limits: gradient flows
+
+
+def test_checker_uses_float64_cosine():
+    a = torch.randn(1 << 16)
+    assert O.cosine(a, a) == pytest.approx(1.0, abs=1e-12)
+    assert O.cosine(a, a) <= 1.0 + 1e-12
