@@ -27,6 +27,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 
 #include "moe_gemm.h"
@@ -533,6 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ============================================================================ host side
 
+static thread_local char g_last_error[256] = "";
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -563,10 +566,14 @@ static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64
     b[i] = box[i];
   }
   for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) {
+    snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    return false;
+  }
+  return true;
 }
 
 struct DeviceInfo {
@@ -586,6 +593,19 @@ static DeviceInfo device_info(int dev) {
   return cache[dev];
 }
 
+static void record_error(const char* what, cudaError_t e) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, cudaGetErrorString(e));
+}
+
+static bool debug_sync() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MGF_DEBUG_SYNC");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 template <int BN, int EPI, bool A_MN, bool B_MN>
 static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid, cudaStream_t st) {
   auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN>;
@@ -597,13 +617,33 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Param
   {
     std::lock_guard<std::mutex> g(mu);
     if (!attr_done[dev]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) {
+        record_error("cudaFuncSetAttribute", e);
         return MGF_ERR_CUDA;
+      }
       attr_done[dev] = true;
     }
   }
+  // A non-sticky error left by an unrelated runtime call would otherwise be reported as ours.
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess && debug_sync()) fprintf(stderr, "[mgf] cleared pre-existing error: %s\n", cudaGetErrorString(e));
   kern<<<grid, kThreads, smem, st>>>(tA, tB, p);
-  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    record_error("kernel launch", e);
+    return MGF_ERR_CUDA;
+  }
+  if (debug_sync()) {
+    e = cudaStreamSynchronize(st);
+    fprintf(stderr, "[mgf] BN=%d epi=%d a_mn=%d b_mn=%d grid=%d E=%d rows=%lld m=%d n=%d k=%d -> %s\n", BN, EPI,
+            int(A_MN), int(B_MN), grid, p.E, (long long)p.total_rows, p.m, p.n, p.k, cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      record_error("kernel execution", e);
+      return MGF_ERR_CUDA;
+    }
+  }
+  return MGF_OK;
 }
 
 template <int BN>
@@ -649,6 +689,8 @@ using namespace mgf;
 
 extern "C" int mgf_version(void) { return 100; }
 
+extern "C" const char* mgf_last_error_detail(void) { return g_last_error; }
+
 extern "C" const char* mgf_status_string(int status) {
   switch (status) {
     case MGF_OK: return "ok";
@@ -686,12 +728,26 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   const mgf_gemm_desc& g = *desc;
   if (g.num_groups < 1 || g.num_groups > kMaxGroups) return MGF_ERR_TOO_MANY_GROUPS;
   if (g.epilogue < MGF_EPI_BIAS || g.epilogue > MGF_EPI_WGRAD) return MGF_ERR_INVALID_ARGUMENT;
-  if (g.offs == nullptr || g.a == nullptr || g.b == nullptr || g.d == nullptr) return MGF_ERR_INVALID_ARGUMENT;
   if (g.total_rows < 0 || g.total_rows > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
   const bool ragged_k = g.epilogue == MGF_EPI_WGRAD;
+  // Ragged-M with no rows has nothing to write.  Ragged-K with no rows still writes zeros for
+  // every group (A and B, possibly NULL, are then never read).
+  if (!ragged_k && g.total_rows == 0) return MGF_OK;
+  const bool no_rows = g.total_rows == 0;
+  if (g.offs == nullptr || g.d == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  if (!no_rows && (g.a == nullptr || g.b == nullptr)) return MGF_ERR_INVALID_ARGUMENT;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MGF_ERR_CUDA;
+  g_last_error[0] = 0;
+  // Tensor maps are encoded through the driver API, which needs a current context on this host
+  // thread.  Threads that only made runtime calls so far (autograd's backward workers) may have
+  // none; cudaSetDevice binds the device's primary context.
+  static thread_local int bound_dev = -1;
+  if (bound_dev != dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) return MGF_ERR_CUDA;
+    bound_dev = dev;
+  }
   const DeviceInfo di = device_info(dev);
   if (di.major != 10) return MGF_ERR_NO_DEVICE_SUPPORT;
 
@@ -717,7 +773,8 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // TMA needs it for A and B, the epilogue's 16-byte vector stores need it for the outputs.
   auto stride_ok = [](int64_t s) { return s > 0 && (s % 8) == 0; };
   if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.d)) return MGF_ERR_ALIGNMENT;
-  if (!stride_ok(g.lda) || !stride_ok(g.ldb) || !stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
+  if (!stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
+  if (!no_rows && (!stride_ok(g.lda) || !stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
 
   CUtensorMap tA, tB;
   int bn, n_tiles;
@@ -771,15 +828,20 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     p.m_tiles_real = static_cast<int>((g.m + BM - 1) / BM);
     p.bias_grad = g.d2 != nullptr ? 1 : 0;
     p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % BM) == 0) ? 1 : 0);
-    const uint64_t rows = static_cast<uint64_t>(g.total_rows > 0 ? g.total_rows : 1);
-    const uint64_t dA[2] = {static_cast<uint64_t>(g.m), rows};
-    const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
-    const uint32_t bA[2] = {64, 64};
-    if (!encode_bf16(&tA, g.a, 2, dA, sA, bA)) return MGF_ERR_CUDA;
-    const uint64_t dB[2] = {static_cast<uint64_t>(g.n), rows};
-    const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb) * 2};
-    const uint32_t bB[2] = {64, 64};
-    if (!encode_bf16(&tB, g.b, 2, dB, sB, bB)) return MGF_ERR_CUDA;
+    const uint32_t box[2] = {64, 64};
+    if (!no_rows) {
+      const uint64_t dA[2] = {static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.total_rows)};
+      const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
+      if (!encode_bf16(&tA, g.a, 2, dA, sA, box)) return MGF_ERR_CUDA;
+      const uint64_t dB[2] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.total_rows)};
+      const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb) * 2};
+      if (!encode_bf16(&tB, g.b, 2, dB, sB, box)) return MGF_ERR_CUDA;
+    } else {
+      // Never dereferenced (every group is empty): well-formed maps over the output buffer.
+      const uint64_t dz[2] = {8, 1};
+      const uint64_t sz[1] = {16};
+      if (!encode_bf16(&tA, g.d, 2, dz, sz, box) || !encode_bf16(&tB, g.d, 2, dz, sz, box)) return MGF_ERR_CUDA;
+    }
     tiles_upper = static_cast<int64_t>(p.m_tiles) * n_tiles * g.num_groups;
   }
 

@@ -21,7 +21,7 @@ namespace {
 using at::Tensor;
 
 void check_launch(int rc, const char* what) {
-  TORCH_CHECK(rc == MGF_OK, what, ": ", mgf_status_string(rc), " (status ", rc, ")");
+  TORCH_CHECK(rc == MGF_OK, what, ": ", mgf_status_string(rc), " (status ", rc, ") ", mgf_last_error_detail());
 }
 
 int64_t padded(int64_t n) { return (n + 7) / 8 * 8; }

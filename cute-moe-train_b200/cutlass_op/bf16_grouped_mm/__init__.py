@@ -11,6 +11,7 @@ import torch
 
 from . import custom_op as _custom_op
 from ._ext import check_device_status, device_status  # noqa: F401
+from .optimer import OpTimer, timed  # noqa: F401
 from .custom_op import (  # noqa: F401
     grouped_mm_downproj_forward,
     grouped_mm_forward,
@@ -56,7 +57,8 @@ def grouped_mm_swiglu(
         ``aux_biased_acc`` must be handed to :func:`grouped_mm_downproj`, which routes the
         gradient back through it; a gradient reaching ``swiglu_out`` directly raises.
     """
-    return torch.ops.grouped_mm.mm_swiglu(mat_a, mat_b, offs, bias, swiglu_alpha, swiglu_limit)
+    with timed("up_swiglu_fwd"):
+        return torch.ops.grouped_mm.mm_swiglu(mat_a, mat_b, offs, bias, swiglu_alpha, swiglu_limit)
 
 
 def grouped_mm_downproj(
@@ -73,9 +75,10 @@ def grouped_mm_downproj(
     Forward equals ``grouped_mm(mat_a, mat_b, offs=offs, bias=bias)``.  Backward computes
     ``grad_aux = SwiGLU_bwd(grad_out @ mat_b^T, aux_biased_acc)`` in one fused launch.
     """
-    return torch.ops.grouped_mm.mm_downproj(
-        mat_a, mat_b, offs, bias, aux_biased_acc, swiglu_alpha, swiglu_limit
-    )
+    with timed("down_fwd"):
+        return torch.ops.grouped_mm.mm_downproj(
+            mat_a, mat_b, offs, bias, aux_biased_acc, swiglu_alpha, swiglu_limit
+        )
 
 
 __all__ = [

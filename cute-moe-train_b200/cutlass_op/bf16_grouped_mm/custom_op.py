@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 
 from . import _ext  # noqa: F401  (loads the native libraries and registers the operators)
+from .optimer import timed
 
 # c10::ScalarType codes accepted by the `out_dtype: int` argument (-1 means "same as mat_a").
 _SCALAR_TYPE_CODE = {torch.float16: 5, torch.float32: 6, torch.bfloat16: 15}
@@ -150,9 +151,11 @@ def _mm_backward(ctx, grad_out):
     if a2 and not b2:
         # ragged-M: out[rows(e)] = a[rows(e)] @ b[e] (+ bias[e])
         if need_a:
-            ga = torch.ops.grouped_mm.mm(grad_out, mat_b.transpose(-2, -1), offs, None, -1)
+            with timed("mm_dgrad"):
+                ga = torch.ops.grouped_mm.mm(grad_out, mat_b.transpose(-2, -1), offs, None, -1)
         if need_b and need_bias:
-            gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_out, offs)
+            with timed("mm_wgrad_bias"):
+                gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_out, offs)
             gbias = gbias.to(ctx.bias_dtype)
         elif need_b:
             gb = torch.ops.grouped_mm.mm(mat_a.transpose(-2, -1), grad_out, offs, None, -1)
@@ -242,9 +245,11 @@ def _swiglu_backward(ctx, grad_swiglu, grad_aux):
     grad_gate_up = grad_aux.contiguous()
     ga = gb = gbias = None
     if need_a:
-        ga = torch.ops.grouped_mm.mm(grad_gate_up, mat_b.transpose(-2, -1), offs, None, -1)
+        with timed("up_dgrad"):
+            ga = torch.ops.grouped_mm.mm(grad_gate_up, mat_b.transpose(-2, -1), offs, None, -1)
     if need_b and need_bias:
-        gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_gate_up, offs)
+        with timed("up_wgrad_bias"):
+            gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_gate_up, offs)
         gbias = gbias.to(ctx.bias_dtype)
     elif need_b:
         gb = torch.ops.grouped_mm.mm(mat_a.transpose(-2, -1), grad_gate_up, offs, None, -1)
@@ -302,16 +307,18 @@ def _downproj_backward(ctx, grad_out):
     grad_out = grad_out.contiguous()
     ga = gb = gbias = gaux = None
     if need_b and need_bias:
-        gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_out, offs)
+        with timed("down_wgrad_bias"):
+            gb, gbias = torch.ops.grouped_mm.mm_wgrad_bias(mat_a.transpose(-2, -1), grad_out, offs)
         gbias = gbias.to(ctx.bias_dtype)
     elif need_b:
         gb = torch.ops.grouped_mm.mm(mat_a.transpose(-2, -1), grad_out, offs, None, -1)
     elif need_bias:
         gbias = segment_sum_rows(grad_out, offs).to(ctx.bias_dtype)
     if need_aux:
-        gaux = torch.ops.grouped_mm.mm_swiglu_bwd(
-            grad_out, mat_b.transpose(-2, -1), offs, aux_biased_acc, ctx.swiglu_alpha, ctx.swiglu_limit
-        )
+        with timed("down_dgrad_swiglu_bwd"):
+            gaux = torch.ops.grouped_mm.mm_swiglu_bwd(
+                grad_out, mat_b.transpose(-2, -1), offs, aux_biased_acc, ctx.swiglu_alpha, ctx.swiglu_limit
+            )
     # With the aux route active the plain dgrad of mat_a is skipped: mm_swiglu's backward
     # consumes grad_aux directly (custom_op.py:681-685).
     if need_a and not need_aux:

@@ -112,6 +112,10 @@ int mgf_device_status(int device, uint32_t* status_out, int clear);
 /* Human-readable text for a mgf_status code. */
 const char* mgf_status_string(int status);
 
+/* Text of the last CUDA / driver error seen by mgf_grouped_gemm_launch on this host thread
+ * ("" when the last call succeeded). */
+const char* mgf_last_error_detail(void);
+
 /* Library ABI version (major * 100 + minor). */
 int mgf_version(void);
 
