@@ -1,0 +1,156 @@
+"""Expert parallelism for the fused MoE FFN: E/N experts per GPU, tokens exchanged with all-to-all.
+
+The reference has no distributed code (its numbers were taken under FSDP without expert
+parallelism, README.md:81-84; compute/communication overlap is on its roadmap, README.md:103-107).
+This module shards the experts over the ranks of a process group, one process per GPU:
+
+forward
+  1. every routed copy (token t, slot j) of the local tokens goes to expert e = expert_idx[t, j],
+     owned by rank e // (E/N); copies are sorted by expert, which also groups them by rank;
+  2. per-(rank, expert) counts are exchanged with a small all-to-all;
+  3. token rows are exchanged with ``all_to_all_single`` (uneven splits) -- dispatch;
+  4. received rows are permuted from (source rank, expert) order into expert order, which yields
+     the int32 ``offs`` of the grouped GEMMs;
+  5. the fused FFN runs on the local experts (grouped_mm_swiglu -> grouped_mm_downproj);
+  6. results return with the inverse all-to-all (combine) and are summed over the top-k slots,
+     optionally weighted by the router probabilities.
+backward mirrors it: the all-to-alls are differentiable (their gradient is the reverse exchange) and
+the expert weight gradients stay local -- pure EP needs no gradient all-reduce.
+
+No kernel reads a peer's memory; all exchanged rows land in this GPU's memory through NCCL first.
+``expert_fn`` can replace the fused FFN (e.g. with a CPU reference for gloo tests of the routing).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+import torch.distributed.nn.functional as dist_fn
+
+
+def route_tokens(tokens: int, num_experts: int, topk: int, routing: str = "zipf", seed: int = 0,
+                 device="cpu", zipf_s: float = 1.1) -> torch.Tensor:
+    """Seeded synthetic router: [tokens, topk] distinct expert ids per token.
+
+    ``uniform`` draws k distinct experts uniformly; ``zipf`` weights expert popularity with
+    Zipf(zipf_s) over a seeded permutation (Gumbel top-k = sampling without replacement).
+    """
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    if routing == "uniform":
+        logw = torch.zeros(num_experts)
+    else:
+        perm = torch.randperm(num_experts, generator=g)
+        w = torch.arange(1, num_experts + 1, dtype=torch.float64).pow(-zipf_s)
+        weights = torch.zeros(num_experts, dtype=torch.float64)
+        weights[perm] = w
+        logw = torch.log(weights).float()
+    u = torch.rand(tokens, num_experts, generator=g).clamp_(1e-12, 1.0 - 1e-7)
+    keys = logw.unsqueeze(0) - torch.log(-torch.log(u))
+    return keys.topk(topk, dim=1).indices.to(device)
+
+
+class DispatchPlan:
+    """Host-side bookkeeping of one dispatch: split sizes and the permutations on the device."""
+
+    def __init__(self, expert_idx: torch.Tensor, num_experts: int, world: int, group=None):
+        device = expert_idx.device
+        T, k = expert_idx.shape
+        self.tokens, self.topk = T, k
+        e_local = num_experts // world
+        self.e_local = e_local
+        flat = expert_idx.reshape(-1).to(torch.int64)
+        # stable sort of the T*k copies by expert id (=> grouped by destination rank as well)
+        self.order = torch.argsort(flat, stable=True)
+        self.copy_token = torch.div(self.order, k, rounding_mode="floor")
+        counts_e = torch.bincount(flat, minlength=num_experts)            # [E] copies per expert
+        send_counts = counts_e.view(world, e_local)                       # [dest rank, local expert]
+        recv_counts = torch.empty_like(send_counts)
+        if world > 1:
+            dist.all_to_all_single(recv_counts.view(-1), send_counts.reshape(-1).contiguous(), group=group)
+        else:
+            recv_counts.copy_(send_counts)
+        # One device->host read of the split sizes (all_to_all_single takes host lists).
+        both = torch.stack([send_counts.sum(1), recv_counts.sum(1)]).cpu()
+        self.send_splits = [int(v) for v in both[0]]
+        self.recv_splits = [int(v) for v in both[1]]
+        self.recv_counts = recv_counts                                    # [src rank, local expert]
+        n_recv = sum(self.recv_splits)
+        self.n_recv = n_recv
+        # received rows are ordered (src rank, expert); the GEMMs want (expert, src rank)
+        seg_key = (torch.arange(e_local, device=device).unsqueeze(0) * world
+                   + torch.arange(world, device=device).unsqueeze(1))     # [src, expert] -> e*world + src
+        row_key = torch.repeat_interleave(seg_key.reshape(-1), recv_counts.reshape(-1), output_size=n_recv)
+        self.to_expert_order = torch.argsort(row_key, stable=True)        # expert-ordered row -> received row
+        per_expert = recv_counts.sum(0)                                   # [local expert]
+        self.offs = torch.cumsum(per_expert, 0).to(torch.int32)
+        self.local_rows = n_recv
+
+
+def _all_to_all(x: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
+    out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
+    return dist_fn.all_to_all_single(out, x.contiguous(), out_splits, in_splits, group=group)
+
+
+def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
+               group=None, router_weights: torch.Tensor | None = None,
+               plan: DispatchPlan | None = None) -> tuple[torch.Tensor, DispatchPlan]:
+    """Expert-parallel MoE FFN over the ranks of ``group``.
+
+    x: [T, H] local tokens; expert_idx: [T, k] global expert ids; expert_fn(rows, offs) -> [rows, H]
+    runs the local experts on expert-ordered rows.  Returns ([T, H] combined output, plan).
+    """
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if num_experts % world:
+        raise RuntimeError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    if plan is None:
+        plan = DispatchPlan(expert_idx, num_experts, world, group)
+    send = x[plan.copy_token]                                             # [T*k, H] sorted by expert
+    recv = _all_to_all(send, plan.recv_splits, plan.send_splits, group) if world > 1 else send
+    rows = recv[plan.to_expert_order]
+    y = expert_fn(rows, plan.offs)
+    back = torch.empty_like(y)
+    back = back.index_copy(0, plan.to_expert_order, y)                    # expert order -> received order
+    ret = _all_to_all(back, plan.send_splits, plan.recv_splits, group) if world > 1 else back
+    if router_weights is not None:
+        w = router_weights.reshape(-1)[plan.order].to(ret.dtype).unsqueeze(1)
+        ret = ret * w
+    out = torch.zeros_like(x).index_add(0, plan.copy_token, ret)
+    return out, plan
+
+
+class EPMoEFFN(torch.nn.Module):
+    """GPT-OSS-style MoE FFN whose E experts are sharded E/N per rank, run with the fused kernels."""
+
+    def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
+                 swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0):
+        super().__init__()
+        from .workloads import MoEShape, make_weights_device
+
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % world:
+            raise RuntimeError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+        self.num_experts, self.group = num_experts, group
+        self.e_local = num_experts // world
+        self.alpha, self.limit = swiglu_alpha, swiglu_limit
+        w_up, b_up, w_down, b_down = make_weights_device(MoEShape(self.e_local, hidden, inter),
+                                                         seed=seed + 7919 * rank, device=device)
+        self.w_up = torch.nn.Parameter(w_up)
+        self.b_up = torch.nn.Parameter(b_up)
+        self.w_down = torch.nn.Parameter(w_down)
+        self.b_down = torch.nn.Parameter(b_down)
+        self.last_local_rows = 0
+
+    def expert_fn(self, rows: torch.Tensor, offs: torch.Tensor) -> torch.Tensor:
+        from . import grouped_mm_downproj, grouped_mm_swiglu
+
+        s, aux = grouped_mm_swiglu(rows, self.w_up, offs, self.b_up, self.alpha, self.limit)
+        return grouped_mm_downproj(s, self.w_down, offs, self.b_down, aux, self.alpha, self.limit)
+
+    def forward(self, x: torch.Tensor, expert_idx: torch.Tensor, router_weights: torch.Tensor | None = None):
+        out, plan = ep_moe_ffn(x, expert_idx, self.num_experts, self.expert_fn, self.group, router_weights)
+        self.last_local_rows = plan.local_rows
+        return out
