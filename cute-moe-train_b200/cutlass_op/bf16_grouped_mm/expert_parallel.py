@@ -117,8 +117,9 @@ def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expe
     if router_weights is not None:
         w = router_weights.reshape(-1)[plan.order].to(ret.dtype).unsqueeze(1)
         ret = ret * w
-    out = torch.zeros_like(x).index_add(0, plan.copy_token, ret)
-    return out, plan
+    # sum the k copies of every token in fp32, round once
+    out = torch.zeros(x.shape, dtype=torch.float32, device=x.device).index_add(0, plan.copy_token, ret.float())
+    return out.to(x.dtype), plan
 
 
 class EPMoEFFN(torch.nn.Module):

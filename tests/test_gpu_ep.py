@@ -1,0 +1,125 @@
+"""Expert parallelism with the fused CUDA FFN: one GPU in-process, two GPUs (NCCL) when visible."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+from oracle import moe_ffn as O
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, T, K = 8, 256, 128, 300, 4
+
+
+def _reference_ffn(x, idx, wu, bu, wd, bd):
+    """Non-EP oracle: every routed copy through its expert (kernel_chain rounding), summed per token."""
+    flat = idx.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    counts = torch.bincount(flat, minlength=wu.shape[0])
+    offs = torch.cumsum(counts, 0).to(torch.int32)
+    rows = x[torch.div(order, idx.shape[1], rounding_mode="floor")]
+    g = torch.zeros(rows.shape[0], wd.shape[-1], dtype=torch.bfloat16)
+    ref = O.kernel_chain(rows, wu, bu, wd, bd, offs, g)
+    y = ref["out"]
+    out = torch.zeros(x.shape[0], x.shape[1]).index_add(0, torch.div(order, idx.shape[1], rounding_mode="floor"), y)
+    return out
+
+
+def test_ep_world1_matches_oracle():
+    from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+    dev = torch.device("cuda", 0)
+    ffn = EPMoEFFN(E, H, I, device=dev, seed=5)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    idx = route_tokens(T, E, K, "zipf", seed=2)
+    xd = x.to(dev).requires_grad_(True)
+    out = ffn(xd, idx.to(dev))
+    out.float().sum().backward()
+    torch.cuda.synchronize()
+    ref = _reference_ffn(x, idx, ffn.w_up.detach().cpu(), ffn.b_up.detach().cpu(), ffn.w_down.detach().cpu(),
+                         ffn.b_down.detach().cpu())
+    r = O.check("ep_out", out.float().cpu(), ref)
+    assert r["ok"], r
+    for p in (xd.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad, ffn.b_down.grad):
+        assert p is not None and torch.isfinite(p.float()).all()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _ep_worker(rank, world, port, q):
+    try:
+        _ep_worker_body(rank, world, port, q)
+    except Exception:  # report instead of leaving the parent waiting
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def _ep_worker_body(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from conftest import PKG  # noqa: F401
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+        ffn = EPMoEFFN(E, H, I, device=dev, seed=5)
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
+        idx = route_tokens(T, E, K, "uniform", seed=20 + rank)
+        out = ffn(x.to(dev), idx.to(dev))
+        torch.cuda.synchronize()
+        # gather every rank's weights so rank 0 can check against a single-process oracle
+        ws = [p.detach() for p in (ffn.w_up, ffn.b_up, ffn.w_down, ffn.b_down)]
+        gathered = []
+        for w in ws:
+            parts = [torch.empty_like(w) for _ in range(world)]
+            dist.all_gather(parts, w)
+            gathered.append(torch.cat(parts, 0).cpu().float().numpy())
+        q.put((rank, x.float().numpy(), idx.numpy(), out.float().cpu().numpy(), gathered))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_world2_nccl_matches_oracle():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=240)
+            assert r[1] != "error", r[2]
+            res[r[0]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for p in procs:
+        assert p.exitcode == 0
+    for rank in range(2):
+        _, x, idx, out, ws = res[rank]
+        wts = [torch.from_numpy(w).to(torch.bfloat16) for w in ws]
+        ref = _reference_ffn(torch.from_numpy(x).to(torch.bfloat16), torch.from_numpy(idx), *wts)
+        r = O.check(f"ep_out_rank{rank}", torch.from_numpy(out), ref)
+        assert r["ok"], r
