@@ -15,11 +15,12 @@
 //   ragged-K weight grad   csrc/grouped_mm_common.cuh:120-133
 //   bias gradient          custom_op.py:79-101 (_segment_sum_rows, fp32 accumulation)
 //
-// Warp roles (192 threads, one CTA per SM):
+// Warp roles (320 threads, one CTA per SM):
 //   warp 0      TMA producer (one elected thread)
 //   warp 1      TMEM allocator + UMMA issuer; for ragged-K it also patches the K tail of the
 //               last stage (zero rows past the group end) and writes the bias-gradient "ones" row
-//   warps 2..5  epilogue: TMEM -> registers -> fused math -> predicated global stores
+//   warps 2..9  epilogue (two warpgroups, each half of the tile's columns): TMEM -> registers ->
+//               fused math -> predicated global stores
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -40,8 +41,10 @@ __device__ unsigned int g_status;
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kMaxGroups = 1024;
-constexpr int kNumEpiWarps = 4;
+constexpr int kEpiGroups = 2;                 // epilogue warpgroups, each owns half of the columns
+constexpr int kNumEpiWarps = 4 * kEpiGroups;
 constexpr int kThreads = 64 + 32 * kNumEpiWarps;
+constexpr int kRing = 4;                      // tile ids in flight between the producer and the consumers
 constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s per pipeline wait
 constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
 
@@ -52,7 +55,7 @@ struct TileCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 384;
   static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + SCHED_BYTES;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -78,6 +81,7 @@ struct Params {
   int64_t ld_aux;
   float alpha, limit;
   int store_aux;
+  int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
 };
 
 struct TileInfo {
@@ -223,8 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* ring_full = bars + 2 * STAGES + 5;
+  uint64_t* ring_empty = bars + 2 * STAGES + 5 + kRing;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* ring_ids = reinterpret_cast<volatile int*>(tmem_holder + 2);
   int* sched = reinterpret_cast<int*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
   SchedSmem ss{sched, sched + (kMaxGroups + 1), sched + 2 * (kMaxGroups + 1)};
 
@@ -241,6 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&tempty_bar[b]), kNumEpiWarps);
     }
     ptx::mbar_init(ptx::smem_u32(drain_bar), 1);
+    for (int j = 0; j < kRing; ++j) {
+      ptx::mbar_init(ptx::smem_u32(&ring_full[j]), 1);
+      ptx::mbar_init(ptx::smem_u32(&ring_empty[j]), 1 + kNumEpiWarps);
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmA);
@@ -266,7 +277,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) { outstanding[s] = false; issued_parity[s] = 0; }
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      // The producer picks the tile sequence (static striding, or an atomic counter when the
+      // launch has one) and hands every tile id to the MMA and epilogue warps through the ring.
+      int t = blockIdx.x;
+      uint32_t rslot = 0, rphase = 0;
+      while (ok) {
+        if (!wait_bounded(ptx::smem_u32(&ring_empty[rslot]), rphase ^ 1, abort_flag)) { ok = false; break; }
+        const int tt = t < total_tiles ? t : -1;
+        ring_ids[rslot] = tt;
+        ptx::mbar_arrive(ptx::smem_u32(&ring_full[rslot]));
+        if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
+        if (tt < 0) break;
         TileInfo ti;
         decode_tile<RAGGED_K>(t, p, ss, ti);
         const int n0 = ti.n_blk * BN;
@@ -296,6 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued_parity[stage] = phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
+        t = (p.tile_counter != nullptr) ? static_cast<int>(gridDim.x) + atomicAdd(p.tile_counter, 1)
+                                        : t + static_cast<int>(gridDim.x);
       }
       if (!ok) {
         // Stopped early: let the copies already in flight land before the CTA exits.
@@ -313,8 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t stage = 0, phase = 0;
     bool ok = true;
     bool issued_any = false;
-    int it = 0;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++it) {
+    uint32_t rslot = 0, rphase = 0;
+    for (int it = 0; ok; ++it) {
+      ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&ring_full[rslot]), rphase, abort_flag));
+      if (!ok) break;
+      const int t = ring_ids[rslot];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ring_empty[rslot]));
+      if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
+      if (t < 0) break;
       TileInfo ti;
       decode_tile<RAGGED_K>(t, p, ss, ti);
       const int buf = it & 1;
@@ -394,26 +424,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Two warpgroups; each reads all 128 TMEM lanes (warp w owns lanes 32*(w%4)..+31, i.e. 32
+    // tile rows) for its half of the tile's columns.
+    const int q = warp & 3;
+    const int wg = (warp - 2) >> 2;
+    constexpr int kChunks = BN / 32 / kEpiGroups;
+    const int c_begin = wg * kChunks;
     const int r = q * 32 + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+    uint32_t rslot = 0, rphase = 0;
+    for (int it = 0;; ++it) {
+      if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&ring_full[rslot]), rphase, abort_flag))) break;
+      const int t = ring_ids[rslot];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ring_empty[rslot]));
+      if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
+      if (t < 0) break;
       TileInfo ti;
       decode_tile<RAGGED_K>(t, p, ss, ti);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
-      if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
-      ptx::tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       const int n0 = ti.n_blk * BN;
 
       if constexpr (!RAGGED_K) {
         const int grow = ti.row0 + r;
         const bool warp_active = ti.row0 + q * 32 < ti.row_end;
         const bool valid = grow < ti.row_end;
+        // SwiGLU backward: the aux words do not depend on the accumulator, so the first chunk's
+        // loads are issued before waiting for the mainloop.
+        uint4 aw[8];
+        if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
+          const int col0 = n0 + c_begin * 32;
+          const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * col0);
+#pragma unroll
+          for (int g = 0; g < 8; ++g) aw[g] = (valid && col0 + 4 * g < p.n) ? __ldg(ap + g) : make_uint4(0, 0, 0, 0);
+        }
+        if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
+        ptx::tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
         if (warp_active) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = c_begin; c < c_begin + kChunks; ++c) {
             const int col0 = n0 + c * 32;
             if (col0 >= p.n) break;
             uint32_t v[32];
@@ -464,17 +514,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                   if (col0 + 16 * g < p.n) sp[g] = make_uint4(so[4 * g], so[4 * g + 1], so[4 * g + 2], so[4 * g + 3]);
               }
             } else if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
-              const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * col0);
+              uint4 cur[8];
+#pragma unroll
+              for (int g = 0; g < 8; ++g) cur[g] = aw[g];
+              // prefetch the next chunk's aux words while this chunk is computed and stored
+              const int ncol0 = col0 + 32;
+              if (c + 1 < c_begin + kChunks && ncol0 < p.n) {
+                const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * ncol0);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) aw[g] = (ncol0 + 4 * g < p.n) ? __ldg(ap + g) : make_uint4(0, 0, 0, 0);
+              }
               uint4* gp = reinterpret_cast<uint4*>(p.d + (int64_t)grow * p.ldd + 2 * col0);
 #pragma unroll
               for (int g = 0; g < 8; ++g) {
                 if (col0 + 4 * g < p.n) {
-                  const uint4 aw = __ldg(ap + g);
                   uint4 o;
-                  o.x = swiglu_bwd_word(__uint_as_float(v[4 * g + 0]), aw.x, p.alpha, p.limit);
-                  o.y = swiglu_bwd_word(__uint_as_float(v[4 * g + 1]), aw.y, p.alpha, p.limit);
-                  o.z = swiglu_bwd_word(__uint_as_float(v[4 * g + 2]), aw.z, p.alpha, p.limit);
-                  o.w = swiglu_bwd_word(__uint_as_float(v[4 * g + 3]), aw.w, p.alpha, p.limit);
+                  o.x = swiglu_bwd_word(__uint_as_float(v[4 * g + 0]), cur[g].x, p.alpha, p.limit);
+                  o.y = swiglu_bwd_word(__uint_as_float(v[4 * g + 1]), cur[g].y, p.alpha, p.limit);
+                  o.z = swiglu_bwd_word(__uint_as_float(v[4 * g + 2]), cur[g].z, p.alpha, p.limit);
+                  o.w = swiglu_bwd_word(__uint_as_float(v[4 * g + 3]), cur[g].w, p.alpha, p.limit);
                   gp[g] = o;
                 }
               }
@@ -482,6 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
+        if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
+        ptx::tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
         // ragged-K weight gradient: rows are output features m0 + r
         const int m0 = ti.m_blk * BM;
         const int frow = m0 + r;
@@ -492,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool warp_active = (m0 + q * 32 < p.m) || (ones_r >= q * 32 && ones_r < q * 32 + 32);
         if (warp_active) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = c_begin; c < c_begin + kChunks; ++c) {
             const int col0 = n0 + c * 32;
             if (col0 >= p.n) break;
             uint32_t packed[16];
@@ -768,6 +829,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.alpha = g.swiglu_alpha;
   p.limit = g.swiglu_limit;
   p.store_aux = g.store_aux;
+  p.tile_counter = g.epilogue == MGF_EPI_WGRAD ? g.workspace : nullptr;
 
   // Every row stride must be a multiple of 8 bf16 (16 bytes) and every base 16-byte aligned:
   // TMA needs it for A and B, the epilogue's 16-byte vector stores need it for the outputs.

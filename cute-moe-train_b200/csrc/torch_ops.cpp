@@ -148,6 +148,9 @@ std::tuple<Tensor, Tensor> ragged_k_launch(const Tensor& mat_a, const Tensor& ma
   g.d = out.data_ptr();
   g.ldd = out.stride(1);
   g.ldd_batch = out.stride(0);
+  // dynamic tile counter of the ragged-K schedule (zero-filled, one per launch)
+  Tensor workspace = at::zeros({1}, mat_a.options().dtype(at::kInt));
+  g.workspace = workspace.data_ptr<int32_t>();
   if (bias_grad) {
     db = at::empty({E, N}, mat_a.options());
     g.d2 = db.data_ptr();

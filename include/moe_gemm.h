@@ -98,6 +98,10 @@ typedef struct mgf_gemm_desc {
   float swiglu_limit;
   int32_t store_aux;     /* SWIGLU: 1 = also write aux (D) */
   int32_t sm_carveout;   /* SMs left free for concurrent work (collectives); 0 = use all */
+  int32_t* workspace;    /* WGRAD: device int32[1], zero-filled before the call: the dynamic tile
+                            counter (tiles of a ragged-K launch cost in proportion to their group's
+                            size; handing them out in order keeps the CTAs on neighbouring tiles).
+                            NULL = static tile striding.  One workspace per launch in flight. */
 } mgf_gemm_desc;
 
 /* Launch one grouped GEMM on `stream` (a cudaStream_t; NULL = legacy default stream).
