@@ -919,3 +919,86 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     default: return dispatch_epi<128>(g.epilogue, b_mn, tA, tB, p, grid, st);
   }
 }
+
+// ============================================================================ allocation-free entry point
+//
+// Some callers cannot allocate device memory at the point where they launch: a runtime that lays out
+// every device buffer once up front (a fixed memory plan with no allocator on the step path), or a
+// host program that binds this C ABI directly and only holds the buffers it was handed.  Such a
+// caller can still pass its inputs and outputs, but has nowhere to get the zero-filled int32 tile
+// counter that the ragged-K weight-gradient launch (MGF_EPI_WGRAD) wants as `workspace`.
+// mgf_grouped_gemm_launch_noalloc runs that launch with the counter taken from the array below
+// instead.  The array lives in the library's device image, so every GPU that loads the library holds
+// its 256 bytes until the process exits.
+//
+// Limits and rules:
+//  * only MGF_EPI_WGRAD descriptors, with desc->workspace == NULL (the entry point supplies it);
+//  * the launch needs one int32 word; a launch needing more than kNoAllocScratchWords words would be
+//    rejected with MGF_ERR_INVALID_ARGUMENT and a message in mgf_last_error_detail();
+//  * every call shares the one array and it keeps the last call's contents, so each call clears the
+//    word it uses (cudaMemsetAsync on `stream`) before the kernel; calls that overlap on the GPU
+//    (different streams, no ordering between them) race on the counter and must not be issued;
+//  * the first call on a device looks up the array's device address (cudaGetSymbolAddress with that
+//    device current) and caches it; make that first call before any stream capture.
+//  * nothing here calls cudaMalloc, cudaFree or any allocating routine.
+
+namespace mgf {
+
+constexpr int kNoAllocScratchWords = 64;
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchWords];
+
+static int32_t* noalloc_scratch_address(int dev) {
+  static int32_t* cached[64] = {};
+  static std::mutex mu;
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (cached[dev] == nullptr) {
+    // The symbol's host-side name is only a stand-in: the device address must come from the
+    // runtime, with this device current.
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      record_error("cudaGetSymbolAddress(g_noalloc_scratch)", e);
+      return nullptr;
+    }
+    cached[dev] = static_cast<int32_t*>(ptr);
+  }
+  return cached[dev];
+}
+
+}  // namespace mgf
+
+extern "C" int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* stream) {
+  if (desc == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  g_last_error[0] = 0;
+  if (desc->epilogue != MGF_EPI_WGRAD) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "mgf_grouped_gemm_launch_noalloc: only MGF_EPI_WGRAD launches use scratch; use mgf_grouped_gemm_launch");
+    return MGF_ERR_INVALID_ARGUMENT;
+  }
+  if (desc->workspace != nullptr) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "mgf_grouped_gemm_launch_noalloc: desc->workspace must be NULL (the static scratch is used)");
+    return MGF_ERR_INVALID_ARGUMENT;
+  }
+  const int words_needed = 1;  // the dynamic tile counter
+  if (words_needed > kNoAllocScratchWords) {
+    snprintf(g_last_error, sizeof(g_last_error),
+             "mgf_grouped_gemm_launch_noalloc: launch needs %d scratch words, the static scratch holds %d",
+             words_needed, kNoAllocScratchWords);
+    return MGF_ERR_INVALID_ARGUMENT;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MGF_ERR_CUDA;
+  int32_t* scratch = noalloc_scratch_address(dev);
+  if (scratch == nullptr) return MGF_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(int32_t) * words_needed, st);
+  if (e != cudaSuccess) {
+    record_error("cudaMemsetAsync(static scratch)", e);
+    return MGF_ERR_CUDA;
+  }
+  mgf_gemm_desc d = *desc;
+  d.workspace = scratch;
+  return mgf_grouped_gemm_launch(&d, stream);
+}

@@ -109,6 +109,18 @@ typedef struct mgf_gemm_desc {
  * csrc/grouped_mm_kernel.cuh:390-486, 760-864, 1267-1390. */
 int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream);
 
+/* Allocation-free variant of the ragged-K weight-gradient launch (MGF_EPI_WGRAD only).
+ * No counterpart in the reference.  For callers that cannot allocate device memory when they
+ * launch (a runtime with a fixed, up-front memory plan; a host program that binds this ABI and
+ * only holds the buffers it was given): the zero-filled tile counter normally passed as
+ * desc->workspace comes instead from a 256-byte static device array inside the library (64 int32
+ * words, 1 used per call; held by every GPU that loads the library until exit).  desc->workspace
+ * must be NULL.  The call clears the word it uses on `stream` before the kernel; all calls share
+ * the array, so calls that overlap on the GPU race and must not be issued.  The first call on a
+ * device looks up the array's address and should come before any stream capture.  Allocates
+ * nothing (no cudaMalloc/cudaFree).  Same return codes as mgf_grouped_gemm_launch. */
+int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* stream);
+
 /* Read (and optionally clear) the device status word of `device`.  Synchronises that
  * device; meant for tests and debugging, never called on the hot path. */
 int mgf_device_status(int device, uint32_t* status_out, int clear);
