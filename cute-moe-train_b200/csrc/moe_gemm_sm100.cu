@@ -48,16 +48,21 @@ constexpr int kRing = 4;                      // tile ids in flight between the 
 constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s per pipeline wait
 constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
 
-template <int BN>
+template <int BN, int CG, bool B_MN>
 struct TileCfg {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_BYTES = BM * BK * 2;                        // this CTA's 128 rows of A
+  static constexpr int BNC = BN / CG;                                // this CTA's columns of B
+  static constexpr int B_CHUNKS = (BNC + 63) / 64;                   // 64-column chunks (MN-major / ragged-K)
+  static constexpr int B_BYTES = B_MN ? B_CHUNKS * 8192 : BNC * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int BAR_BYTES = 384;
   static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
+  static constexpr int BUDGET = 227 * 1024 - 1024 - BAR_BYTES - SCHED_BYTES;
+  static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + SCHED_BYTES;
+  static_assert(STAGES >= 3, "pipeline depth");
+  static_assert((3 * STAGES + 5 + 2 * kRing) * 8 + 16 <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -68,7 +73,7 @@ struct Params {
   int m, n, k;
   int n_tiles;
   int m_tiles;        // ragged-K: tiles along m per group (incl. the extra bias-grad tile)
-  int m_tiles_real;   // ragged-K: ceil(m / BM)
+  int m_tiles_real;   // ragged-K: ceil(m / tile rows)
   int bias_grad;      // ragged-K: write D2
   const int32_t* offs;
   const __nv_bfloat16* bias;
@@ -98,13 +103,22 @@ struct SchedSmem {
   int* seg_end;    // [E]
 };
 
+template <bool CLUSTER = false>
+__device__ __forceinline__ bool try_wait_sel(uint32_t bar, uint32_t parity) {
+  if constexpr (CLUSTER) return ptx::mbar_try_wait_cluster(bar, parity);
+  return ptx::mbar_try_wait(bar, parity);
+}
+
+// Wait for phase `parity` of an mbarrier for at most `limit_ns`.  CLUSTER = true acquires at
+// cluster scope (barriers that the peer CTA of a pair also arrives on).
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                              uint64_t limit_ns = kWaitLimitNs) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+  if (try_wait_sel<CLUSTER>(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
   uint32_t it = 0;
   while (true) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (try_wait_sel<CLUSTER>(bar, parity)) return true;
     if ((++it & 127u) == 0) {
       if (*abort_flag) return false;
       if (ptx::globaltimer_ns() - t0 > limit_ns) {
@@ -116,7 +130,7 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
   }
 }
 
-template <bool RAGGED_K>
+template <int TM, bool RAGGED_K>
 __device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedSmem& s, TileInfo& ti) {
   int lo = 0, hi = p.E;
   while (hi - lo > 1) {
@@ -128,7 +142,7 @@ __device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedS
   ti.m_blk = local / p.n_tiles;
   ti.n_blk = local - ti.m_blk * p.n_tiles;
   if constexpr (!RAGGED_K) {
-    ti.row0 = s.seg_start[lo] + ti.m_blk * BM;
+    ti.row0 = s.seg_start[lo] + ti.m_blk * TM;
     ti.row_end = s.seg_end[lo];
     ti.k_start = 0;
     ti.k_end = p.k;
@@ -145,7 +159,7 @@ __device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedS
 // Clamp every group's [start, end) into [0, total_rows] and build the tile prefix.  Malformed
 // offs (decreasing, negative, or past total_rows) are reported through g_status, never by a
 // trap; the clamped segments keep every access in bounds.  Run by one warp.
-template <int BN, bool RAGGED_K>
+template <int TM, bool RAGGED_K>
 __device__ void build_schedule(const Params& p, const SchedSmem& s, int lane) {
   int running = 0;
   bool bad = false;
@@ -162,7 +176,7 @@ __device__ void build_schedule(const Params& p, const SchedSmem& s, int lane) {
       s.seg_start[e] = (int)sp;
       s.seg_end[e] = (int)ep;
       if constexpr (!RAGGED_K) {
-        cnt = (int)((ep - sp + BM - 1) / BM) * p.n_tiles;
+        cnt = (int)((ep - sp + TM - 1) / TM) * p.n_tiles;
       } else {
         cnt = p.m_tiles * p.n_tiles;
       }
@@ -210,13 +224,47 @@ __device__ __forceinline__ uint32_t swiglu_bwd_word(float gs, uint32_t aux_word,
   return pack_bf16x2(d_gate, d_up);
 }
 
-template <int BN, int EPI, bool A_MN, bool B_MN>
+// Zero the K rows past the group end in this CTA's A and B chunks of one stage (each K row is one
+// 128-byte line of a 64-column chunk, whatever the swizzle) and set the bias-gradient "ones" row of
+// A for the valid K rows.  Run by one warp; the caller fences the writes to the async proxy.
+template <int A_CHUNKS, int B_CHUNKS>
+__device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, int ones_local, int lane) {
+  constexpr int kChunks = A_CHUNKS + B_CHUNKS;
+  const int nrows = BK - valid_k;
+  const int n16 = nrows * 8 * kChunks;
+  for (int i = lane; i < n16; i += 32) {
+    const int chunk = i / (nrows * 8);
+    const int rem = i - chunk * nrows * 8;
+    const int row = valid_k + rem / 8;
+    const int col16 = rem & 7;
+    *reinterpret_cast<uint4*>(sA + chunk * 8192 + row * 128 + col16 * 16) = make_uint4(0, 0, 0, 0);
+  }
+  if (ones_local >= 0) {
+    // The A feature row past m reads as zero (TMA out-of-bounds fill); 1.0 in its valid K rows makes
+    // accumulator row `ones_local` the column sums of B.  128-byte swizzle: 16-byte unit ^= row % 8.
+    const int c1 = ones_local >> 6, mm = ones_local & 63;
+    for (int kr = lane; kr < valid_k; kr += 32) {
+      const int off = c1 * 8192 + kr * 128 + (((mm >> 3) ^ (kr & 7)) << 4) + (mm & 7) * 2;
+      *reinterpret_cast<uint16_t*>(sA + off) = 0x3F80u;
+    }
+  }
+}
+
+// CG = 1: one CTA per 128 x BN tile.  CG = 2: a cluster of two CTAs per 256 x BN tile; the even
+// CTA issues tcgen05.mma.cta_group::2 over both CTAs' shared memory (each CTA holds 128 rows of A
+// and BN/2 columns of B) and both CTAs' TMEM (each holds its 128 rows of the accumulator).
+// Stages whose odd-CTA half must be patched first (ragged-K tails, the ones row) are "relayed":
+// the odd CTA counts their bytes on its own barrier, patches, then arrives on the even CTA's
+// patch_done barrier; every other stage counts both CTAs' bytes directly on the even CTA's barrier.
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const Params p) {
-  using Cfg = TileCfg<BN>;
+  using Cfg = TileCfg<BN, CG, B_MN>;
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int TM = BM * CG;   // rows of a tile
+  constexpr int BNC = BN / CG;  // B columns held by one CTA
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -229,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain_bar = bars + 2 * STAGES + 4;
   uint64_t* ring_full = bars + 2 * STAGES + 5;
   uint64_t* ring_empty = bars + 2 * STAGES + 5 + kRing;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5 + 2 * kRing);
+  uint64_t* patch_done = bars + 2 * STAGES + 5 + 2 * kRing;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5 + 2 * kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* ring_ids = reinterpret_cast<volatile int*>(tmem_holder + 2);
   int* sched = reinterpret_cast<int*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
@@ -237,15 +286,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t crank = (CG == 2) ? ptx::cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
+  const int unit = (CG == 2) ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int num_units = (CG == 2) ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(ptx::smem_u32(&full_bar[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&empty_bar[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&patch_done[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(ptx::smem_u32(&tfull_bar[b]), 1);
-      ptx::mbar_init(ptx::smem_u32(&tempty_bar[b]), kNumEpiWarps);
+      ptx::mbar_init(ptx::smem_u32(&tempty_bar[b]), kNumEpiWarps * CG);
     }
     ptx::mbar_init(ptx::smem_u32(drain_bar), 1);
     for (int j = 0; j < kRing; ++j) {
@@ -258,19 +312,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
-    ptx::tmem_relinquish();
+    if constexpr (CG == 2) {
+      ptx::tmem_alloc_pair(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
+      ptx::tmem_relinquish();
+    }
   }
-  if (warp == 2) build_schedule<BN, RAGGED_K>(p, ss, lane);
+  if (warp == 2) build_schedule<TM, RAGGED_K>(p, ss, lane);
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();  // barriers of both CTAs initialised before any remote use
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int total_tiles = ss.prefix[p.E];
 
+  // Shared::cluster address of a barrier in the even CTA (identity for CG = 1).
+  auto leader_addr = [&](const void* ptr) -> uint32_t {
+    const uint32_t a = ptx::smem_u32(ptr);
+    if constexpr (CG == 2) return ptx::mapa_shared(a, 0);
+    return a;
+  };
+  // Does the odd CTA of a ragged-K pair hold the ones row of this tile?
+  auto odd_has_ones = [&](const TileInfo& ti) -> bool {
+    if constexpr (CG == 2 && RAGGED_K) {
+      const int o = p.m - ti.m_blk * TM - BM;
+      return p.bias_grad && o >= 0 && o < BM;
+    }
+    return false;
+  };
+  // Stages relayed through the odd CTA (CG = 2, ragged-K): those it must patch before the MMA.
+  auto relayed = [&](const TileInfo& ti, int kb, bool odd_ones) -> bool {
+    if constexpr (CG == 2 && RAGGED_K) {
+      const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
+      return valid_k < BK || odd_ones;
+    }
+    return false;
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      constexpr uint32_t kLoadBytes = Cfg::STAGE_BYTES;  // bytes landing in this CTA per stage
       uint32_t stage = 0, phase = 0;
       uint32_t issued_parity[STAGES];
       bool outstanding[STAGES];
@@ -279,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // The producer picks the tile sequence (static striding, or an atomic counter when the
       // launch has one) and hands every tile id to the MMA and epilogue warps through the ring.
-      int t = blockIdx.x;
+      int t = unit;
       uint32_t rslot = 0, rphase = 0;
       while (ok) {
         if (!wait_bounded(ptx::smem_u32(&ring_empty[rslot]), rphase ^ 1, abort_flag)) { ok = false; break; }
@@ -289,51 +373,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
         if (tt < 0) break;
         TileInfo ti;
-        decode_tile<RAGGED_K>(t, p, ss, ti);
-        const int n0 = ti.n_blk * BN;
+        decode_tile<TM, RAGGED_K>(t, p, ss, ti);
+        const bool odd_ones = odd_has_ones(ti);
+        const int nb0 = ti.n_blk * BN + static_cast<int>(crank) * BNC;  // this CTA's first B column
         for (int kb = 0; kb < ti.nk; ++kb) {
           if (!wait_bounded(ptx::smem_u32(&empty_bar[stage]), phase ^ 1, abort_flag)) { ok = false; break; }
-          const uint32_t fb = ptx::smem_u32(&full_bar[stage]);
-          ptx::mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          const uint32_t own_full = ptx::smem_u32(&full_bar[stage]);
+          uint32_t fb = own_full;
+          if constexpr (CG == 2) {
+            const bool relay = relayed(ti, kb, odd_ones);
+            if (leader) {
+              ptx::mbar_arrive_expect_tx(own_full, relay ? kLoadBytes : 2 * kLoadBytes);
+            } else if (relay) {
+              ptx::mbar_arrive_expect_tx(own_full, kLoadBytes);
+            } else {
+              fb = leader_addr(&full_bar[stage]);
+            }
+          } else {
+            ptx::mbar_arrive_expect_tx(own_full, kLoadBytes);
+          }
           const uint32_t sA = ptx::smem_u32(stage_base + stage * Cfg::STAGE_BYTES);
           const uint32_t sB = sA + Cfg::A_BYTES;
+          auto load2 = [&](uint32_t dst, const CUtensorMap* tm, int x, int y) {
+            if constexpr (CG == 2) ptx::tma_load_2d_pair(dst, tm, fb, x, y);
+            else ptx::tma_load_2d(dst, tm, fb, x, y);
+          };
+          auto load3 = [&](uint32_t dst, const CUtensorMap* tm, int x, int y, int z) {
+            if constexpr (CG == 2) ptx::tma_load_3d_pair(dst, tm, fb, x, y, z);
+            else ptx::tma_load_3d(dst, tm, fb, x, y, z);
+          };
           if constexpr (!RAGGED_K) {
-            ptx::tma_load_2d(sA, &tmA, fb, kb * BK, ti.row0);
+            load2(sA, &tmA, kb * BK, ti.row0 + static_cast<int>(crank) * BM);
             if constexpr (B_MN) {
 #pragma unroll
-              for (int c = 0; c < BN / 64; ++c) ptx::tma_load_3d(sB + c * 8192, &tmB, fb, n0 + 64 * c, kb * BK, ti.e);
+              for (int c = 0; c < Cfg::B_CHUNKS; ++c) load3(sB + c * 8192, &tmB, nb0 + 64 * c, kb * BK, ti.e);
             } else {
-              ptx::tma_load_3d(sB, &tmB, fb, kb * BK, n0, ti.e);
+              load3(sB, &tmB, kb * BK, nb0, ti.e);
             }
           } else {
             const int kr = ti.k_start + kb * BK;
-            const int m0 = ti.m_blk * BM;
+            const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c) ptx::tma_load_2d(sA + c * 8192, &tmA, fb, m0 + 64 * c, kr);
+            for (int c = 0; c < BM / 64; ++c) load2(sA + c * 8192, &tmA, m0 + 64 * c, kr);
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) ptx::tma_load_2d(sB + c * 8192, &tmB, fb, n0 + 64 * c, kr);
+            for (int c = 0; c < Cfg::B_CHUNKS; ++c) load2(sB + c * 8192, &tmB, nb0 + 64 * c, kr);
           }
           outstanding[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        t = (p.tile_counter != nullptr) ? static_cast<int>(gridDim.x) + atomicAdd(p.tile_counter, 1)
-                                        : t + static_cast<int>(gridDim.x);
+        t = (p.tile_counter != nullptr) ? num_units + atomicAdd(p.tile_counter, 1) : t + num_units;
       }
-      if (!ok) {
-        // Stopped early: let the copies already in flight land before the CTA exits.
+      if (!ok && CG == 1) {
+        // Stopped early: let the copies already in flight land before the CTA exits.  (A pair waits
+        // for its copies at the final cluster barrier.)
         for (int s = 0; s < STAGES; ++s)
           if (outstanding[s]) wait_bounded(ptx::smem_u32(&full_bar[s]), issued_parity[s], abort_flag, kDrainLimitNs);
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer
-    constexpr uint32_t idesc = ptx::make_idesc_bf16(BM, BN, A_MN, B_MN);
+    // ------------------------------------------------------------ UMMA issuer (even CTA) /
+    //                                                              ragged-K stage patcher (odd CTA)
+    constexpr uint32_t idesc = ptx::make_idesc_bf16(TM, BN, A_MN, B_MN);
     constexpr uint32_t a_lbo = A_MN ? 8192u : 16u;
     constexpr uint32_t b_lbo = B_MN ? 8192u : 16u;
     constexpr uint32_t a_kstep = A_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
     constexpr uint32_t b_kstep = B_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
+    const bool issuer = (CG == 1) || leader;
     uint32_t stage = 0, phase = 0;
+    uint32_t relay_bits = 0;  // per-stage phase of patch_done (even CTA) / own full (odd CTA) on relayed stages
     bool ok = true;
     bool issued_any = false;
     uint32_t rslot = 0, rphase = 0;
@@ -345,51 +453,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ring_empty[rslot]));
       if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
       if (t < 0) break;
+      if (!issuer && !RAGGED_K) continue;  // the odd CTA of a ragged-M pair has nothing to do here
       TileInfo ti;
-      decode_tile<RAGGED_K>(t, p, ss, ti);
+      decode_tile<TM, RAGGED_K>(t, p, ss, ti);
+      const bool odd_ones = odd_has_ones(ti);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
-      ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tempty_bar[buf]), tph ^ 1, abort_flag));
-      if (!ok) break;
-      ptx::tc_fence_after();
+      if (issuer) {
+        ok = __all_sync(0xffffffffu,
+                        wait_bounded<CG == 2>(ptx::smem_u32(&tempty_bar[buf]), tph ^ 1, abort_flag));
+        if (!ok) break;
+        ptx::tc_fence_after();
+      }
       const uint32_t d_tmem = tmem_base + buf * BN;
-      int ones_r = -1;
+      int ones_local = -1;  // this CTA's A row that carries the bias-gradient ones
       if constexpr (RAGGED_K) {
         if (p.bias_grad) {
-          const int m0 = ti.m_blk * BM;
-          if (p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
+          const int o = p.m - ti.m_blk * TM - static_cast<int>(crank) * BM;
+          if (o >= 0 && o < BM) ones_local = o;
         }
       }
       for (int kb = 0; kb < ti.nk; ++kb) {
-        ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), phase, abort_flag));
-        if (!ok) break;
-        ptx::tc_fence_after();
         uint8_t* sA_ptr = stage_base + stage * Cfg::STAGE_BYTES;
+        const bool relay = relayed(ti, kb, odd_ones);
+        if (!issuer) {
+          // odd CTA of a ragged-K pair: patch the relayed stages, then release them to the leader
+          if (relay) {
+            const uint32_t par = (relay_bits >> stage) & 1u;
+            relay_bits ^= 1u << stage;
+            ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), par, abort_flag));
+            if (!ok) break;
+            const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive_cluster(leader_addr(&patch_done[stage]));
+          }
+          __syncwarp();
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          continue;
+        }
+        ok = __all_sync(0xffffffffu, wait_bounded<CG == 2>(ptx::smem_u32(&full_bar[stage]), phase, abort_flag));
+        if (!ok) break;
+        if (relay) {
+          const uint32_t par = (relay_bits >> stage) & 1u;
+          relay_bits ^= 1u << stage;
+          ok = __all_sync(0xffffffffu, wait_bounded<true>(ptx::smem_u32(&patch_done[stage]), par, abort_flag));
+          if (!ok) break;
+        }
+        ptx::tc_fence_after();
         if constexpr (RAGGED_K) {
           const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
-          if (valid_k < BK || ones_r >= 0) {
-            // Zero the K rows past the group end (they hold the next group's tokens),
-            // in every 64-column chunk of A and B.  Each K row is one 128-byte line.
-            constexpr int kChunks = BM / 64 + BN / 64;
-            const int nrows = BK - valid_k;
-            const int n16 = nrows * 8 * kChunks;
-            for (int i = lane; i < n16; i += 32) {
-              const int chunk = i / (nrows * 8);
-              const int rem = i - chunk * nrows * 8;
-              const int row = valid_k + rem / 8;
-              const int col16 = rem & 7;
-              uint8_t* base = sA_ptr + chunk * 8192;  // A chunks then B chunks are contiguous
-              *reinterpret_cast<uint4*>(base + row * 128 + col16 * 16) = make_uint4(0, 0, 0, 0);
-            }
-            if (ones_r >= 0) {
-              // A feature row past m reads as zero (TMA out-of-bounds fill); set it to 1.0 for
-              // the valid K rows so accumulator row ones_r receives the column sums of B.
-              const int c1 = ones_r >> 6, mm = ones_r & 63;
-              for (int kr = lane; kr < valid_k; kr += 32) {
-                const int off = c1 * 8192 + kr * 128 + ((((mm >> 3) ^ (kr & 7))) << 4) + (mm & 7) * 2;
-                *reinterpret_cast<uint16_t*>(sA_ptr + off) = 0x3F80u;
-              }
-            }
+          if (valid_k < BK || ones_local >= 0) {
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -401,24 +517,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if constexpr (CG == 2) {
+              ptx::umma_bf16_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+            } else {
+              ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
-          ptx::umma_commit(ptx::smem_u32(&empty_bar[stage]));
+          if constexpr (CG == 2) ptx::umma_commit_pair(ptx::smem_u32(&empty_bar[stage]), 0x3);
+          else ptx::umma_commit(ptx::smem_u32(&empty_bar[stage]));
           issued_any = true;
         }
         __syncwarp();
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
-      if (lane == 0) {
-        if (ti.nk > 0) ptx::umma_commit(ptx::smem_u32(&tfull_bar[buf]));
-        else ptx::mbar_arrive(ptx::smem_u32(&tfull_bar[buf]));
+      if (issuer && lane == 0) {
+        if (ti.nk > 0) {
+          if constexpr (CG == 2) ptx::umma_commit_pair(ptx::smem_u32(&tfull_bar[buf]), 0x3);
+          else ptx::umma_commit(ptx::smem_u32(&tfull_bar[buf]));
+        } else {
+          // empty group (ragged-K): nothing to multiply, the epilogues write zeros
+          ptx::mbar_arrive(ptx::smem_u32(&tfull_bar[buf]));
+          if constexpr (CG == 2) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tfull_bar[buf]), 1));
+        }
       }
       __syncwarp();
     }
-    if (!ok && lane == 0 && issued_any) {
+    if (!ok && issuer && lane == 0 && issued_any) {
       // Stopped early: wait for the UMMAs already issued before TMEM is released.
-      ptx::umma_commit(ptx::smem_u32(drain_bar));
+      if constexpr (CG == 2) ptx::umma_commit_pair(ptx::smem_u32(drain_bar), 0x1);
+      else ptx::umma_commit(ptx::smem_u32(drain_bar));
       wait_bounded(ptx::smem_u32(drain_bar), 0, abort_flag, kDrainLimitNs);
     }
     __syncwarp();
@@ -431,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunks = BN / 32 / kEpiGroups;
     const int c_begin = wg * kChunks;
     const int r = q * 32 + lane;
+    const uint32_t tempty_leader[2] = {leader_addr(&tempty_bar[0]), leader_addr(&tempty_bar[1])};
     uint32_t rslot = 0, rphase = 0;
     for (int it = 0;; ++it) {
       if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&ring_full[rslot]), rphase, abort_flag))) break;
@@ -440,14 +569,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
       if (t < 0) break;
       TileInfo ti;
-      decode_tile<RAGGED_K>(t, p, ss, ti);
+      decode_tile<TM, RAGGED_K>(t, p, ss, ti);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
       const int n0 = ti.n_blk * BN;
 
       if constexpr (!RAGGED_K) {
-        const int grow = ti.row0 + r;
-        const bool warp_active = ti.row0 + q * 32 < ti.row_end;
+        const int crow0 = ti.row0 + static_cast<int>(crank) * BM;  // first row of this CTA's half
+        const int grow = crow0 + r;
+        const bool warp_active = crow0 + q * 32 < ti.row_end;
         const bool valid = grow < ti.row_end;
         // SwiGLU backward: the aux words do not depend on the accumulator, so the first chunk's
         // loads are issued before waiting for the mainloop.
@@ -544,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
         // ragged-K weight gradient: rows are output features m0 + r
-        const int m0 = ti.m_blk * BM;
+        const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
         const int frow = m0 + r;
         int ones_r = -1;
         if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
@@ -581,15 +711,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&tempty_bar[buf]));
+      if (lane == 0) {
+        if constexpr (CG == 2) ptx::mbar_arrive_cluster(tempty_leader[buf]);
+        else ptx::mbar_arrive(ptx::smem_u32(&tempty_bar[buf]));
+      }
     }
   }
 
   ptx::tc_fence_before();
   __syncthreads();
+  // A pair leaves together: the peer may still signal this CTA's barriers until both are done.
+  if constexpr (CG == 2) ptx::cluster_sync();
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (CG == 2) ptx::tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -667,38 +803,66 @@ static bool debug_sync() {
   return v == 1;
 }
 
-template <int BN, int EPI, bool A_MN, bool B_MN>
-static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid, cudaStream_t st) {
-  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN>;
-  constexpr int smem = TileCfg<BN>::SMEM_BYTES;
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
+static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid_in, cudaStream_t st) {
+  int grid = grid_in;
+  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG>;
+  constexpr int smem = TileCfg<BN, CG, B_MN>::SMEM_BYTES;
   static std::mutex mu;
   static bool attr_done[64] = {};
+  static int max_clusters[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MGF_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   {
     std::lock_guard<std::mutex> g(mu);
     if (!attr_done[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) {
         record_error("cudaFuncSetAttribute", e);
         return MGF_ERR_CUDA;
       }
+      if (CG == 2) {
+        // Persistent pairs: never launch more clusters than can be resident at once, or the extra
+        // ones would start only after others finished their whole share of tiles.
+        cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = 1 << 30;
+        cudaGetLastError();
+        max_clusters[dev] = n;
+      }
       attr_done[dev] = true;
     }
   }
+  if (CG == 2 && grid / 2 > max_clusters[dev]) grid = 2 * max_clusters[dev];
   // A non-sticky error left by an unrelated runtime call would otherwise be reported as ours.
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess && debug_sync()) fprintf(stderr, "[mgf] cleared pre-existing error: %s\n", cudaGetErrorString(e));
-  kern<<<grid, kThreads, smem, st>>>(tA, tB, p);
-  e = cudaGetLastError();
+  if constexpr (CG == 1) {
+    kern<<<grid, kThreads, smem, st>>>(tA, tB, p);
+    e = cudaGetLastError();
+  } else {
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p);
+  }
   if (e != cudaSuccess) {
     record_error("kernel launch", e);
     return MGF_ERR_CUDA;
   }
   if (debug_sync()) {
     e = cudaStreamSynchronize(st);
-    fprintf(stderr, "[mgf] BN=%d epi=%d a_mn=%d b_mn=%d grid=%d E=%d rows=%lld m=%d n=%d k=%d -> %s\n", BN, EPI,
-            int(A_MN), int(B_MN), grid, p.E, (long long)p.total_rows, p.m, p.n, p.k, cudaGetErrorString(e));
+    fprintf(stderr, "[mgf] BN=%d CG=%d epi=%d a_mn=%d b_mn=%d grid=%d E=%d rows=%lld m=%d n=%d k=%d -> %s\n", BN, CG,
+            EPI, int(A_MN), int(B_MN), grid, p.E, (long long)p.total_rows, p.m, p.n, p.k, cudaGetErrorString(e));
     if (e != cudaSuccess) {
       record_error("kernel execution", e);
       return MGF_ERR_CUDA;
@@ -707,24 +871,34 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Param
   return MGF_OK;
 }
 
-template <int BN>
+template <int BN, int CG>
 static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid,
                         cudaStream_t st) {
   switch (epi) {
     case MGF_EPI_BIAS:
-      return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_BIAS, false, false>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true, CG>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_BIAS, false, false, CG>(tA, tB, p, grid, st);
     case MGF_EPI_SWIGLU:
-      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU, false, true>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_SWIGLU, false, false>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU, false, true, CG>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU, false, false, CG>(tA, tB, p, grid, st);
     case MGF_EPI_SWIGLU_BWD:
-      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true, CG>(tA, tB, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false, CG>(tA, tB, p, grid, st);
     case MGF_EPI_WGRAD:
-      return launch_inst<BN, MGF_EPI_WGRAD, true, true>(tA, tB, p, grid, st);
+      return launch_inst<BN, MGF_EPI_WGRAD, true, true, CG>(tA, tB, p, grid, st);
     default:
       return MGF_ERR_INVALID_ARGUMENT;
   }
+}
+
+// CTA pair (cta_group::2, 256-row tiles) or single CTA (128-row tiles).  Pairs halve the B bytes
+// each SM streams per FLOP; their 256-row tiles waste more rows at group ends, so small groups stay
+// on single CTAs.  MGF_CTA_GROUP=1|2 forces a choice (the tests exercise both).
+static int pick_cta_group(bool ragged_k, int64_t total_rows, int num_groups, int64_t m) {
+  const char* env = getenv("MGF_CTA_GROUP");
+  if (env != nullptr && (env[0] == '1' || env[0] == '2')) return env[0] - '0';
+  if (!ragged_k) return (total_rows / num_groups >= 512) ? 2 : 1;
+  return m >= 512 ? 2 : 1;
 }
 
 // N tile: the candidate with the least padding along n, ties to the wider tile.
@@ -829,7 +1003,6 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.alpha = g.swiglu_alpha;
   p.limit = g.swiglu_limit;
   p.store_aux = g.store_aux;
-  p.tile_counter = g.epilogue == MGF_EPI_WGRAD ? g.workspace : nullptr;
 
   // Every row stride must be a multiple of 8 bf16 (16 bytes) and every base 16-byte aligned:
   // TMA needs it for A and B, the epilogue's 16-byte vector stores need it for the outputs.
@@ -839,7 +1012,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   if (!no_rows && (!stride_ok(g.lda) || !stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
 
   CUtensorMap tA, tB;
-  int bn, n_tiles;
+  int bn, n_tiles, cg = 1;
   int64_t tiles_upper;
   if (!ragged_k) {
     if (g.n <= 0 || g.k <= 0 || (g.n % 8) != 0 || (g.k % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
@@ -861,6 +1034,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     n_tiles = static_cast<int>((g.n + bn - 1) / bn);
     p.n_tiles = n_tiles;
     if (g.total_rows == 0) return MGF_OK;  // nothing to compute, outputs have no rows
+    cg = pick_cta_group(false, g.total_rows, g.num_groups, 0);
     const uint64_t dA[2] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.total_rows)};
     const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
     const uint32_t bA[2] = {64, 128};
@@ -872,10 +1046,10 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
       if (!encode_bf16(&tB, g.b, 3, dB, sB, bB)) return MGF_ERR_CUDA;
     } else {
       const uint64_t dB[3] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.num_groups)};
-      const uint32_t bB[3] = {64, static_cast<uint32_t>(bn), 1};
+      const uint32_t bB[3] = {64, static_cast<uint32_t>(bn / cg), 1};
       if (!encode_bf16(&tB, g.b, 3, dB, sB, bB)) return MGF_ERR_CUDA;
     }
-    tiles_upper = (g.total_rows / BM + g.num_groups) * static_cast<int64_t>(n_tiles);
+    tiles_upper = (g.total_rows / (BM * cg) + g.num_groups) * static_cast<int64_t>(n_tiles);
   } else {
     if (g.m <= 0 || g.n <= 0 || (g.m % 8) != 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
     if (g.m > INT32_MAX || g.n > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
@@ -887,9 +1061,11 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     bn = pick_bn(g.n);
     n_tiles = static_cast<int>((g.n + bn - 1) / bn);
     p.n_tiles = n_tiles;
-    p.m_tiles_real = static_cast<int>((g.m + BM - 1) / BM);
+    cg = pick_cta_group(true, g.total_rows, g.num_groups, g.m);
+    const int tm = BM * cg;
+    p.m_tiles_real = static_cast<int>((g.m + tm - 1) / tm);
     p.bias_grad = g.d2 != nullptr ? 1 : 0;
-    p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % BM) == 0) ? 1 : 0);
+    p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % tm) == 0) ? 1 : 0);
     const uint32_t box[2] = {64, 64};
     if (!no_rows) {
       const uint64_t dA[2] = {static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.total_rows)};
@@ -908,15 +1084,27 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   }
 
   int sms = di.sms - (g.sm_carveout > 0 ? g.sm_carveout : 0);
-  if (sms < 1) sms = 1;
-  const int grid = static_cast<int>(tiles_upper < sms ? tiles_upper : sms);
-  if (grid <= 0) return MGF_OK;
+  if (sms < cg) sms = cg;
+  const int units = sms / cg;  // CTAs (CG = 1) or CTA pairs (CG = 2) resident at once
+  const int64_t launch_units = tiles_upper < units ? tiles_upper : units;
+  if (launch_units <= 0) return MGF_OK;
+  const int grid = static_cast<int>(launch_units) * cg;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool b_mn = ragged_k ? true : (g.b_mn_major != 0);
+  // The dynamic tile counter serves single CTAs only: both CTAs of a pair must walk the same tile
+  // sequence, which static striding gives them.
+  p.tile_counter = (g.epilogue == MGF_EPI_WGRAD && cg == 1) ? g.workspace : nullptr;
+  if (cg == 2) {
+    switch (bn) {
+      case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
+      case 192: return dispatch_epi<192, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
+      default: return dispatch_epi<128, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    }
+  }
   switch (bn) {
-    case 256: return dispatch_epi<256>(g.epilogue, b_mn, tA, tB, p, grid, st);
-    case 192: return dispatch_epi<192>(g.epilogue, b_mn, tA, tB, p, grid, st);
-    default: return dispatch_epi<128>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    case 256: return dispatch_epi<256, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    case 192: return dispatch_epi<192, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    default: return dispatch_epi<128, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
   }
 }
 
