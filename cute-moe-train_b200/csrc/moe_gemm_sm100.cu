@@ -897,8 +897,12 @@ static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtenso
 static int pick_cta_group(bool ragged_k, int64_t total_rows, int num_groups, int64_t m) {
   const char* env = getenv("MGF_CTA_GROUP");
   if (env != nullptr && (env[0] == '1' || env[0] == '2')) return env[0] - '0';
+  (void)m;
   if (!ragged_k) return (total_rows / num_groups >= 512) ? 2 : 1;
-  return m >= 512 ? 2 : 1;
+  // Ragged-K pairs measured slower than single CTAs with the dynamic tile order (B200, cfg3 shapes:
+  // 2.5 vs 2.07 ms and 4.8 vs 4.06 ms): m = 2880 wastes 6.7% of a 256-row tile and pairs must use
+  // static striding.  MGF_CTA_GROUP=2 still selects them.
+  return 1;
 }
 
 // N tile: the candidate with the least padding along n, ties to the wider tile.
