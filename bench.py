@@ -50,7 +50,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["auto", "cfg3", "cfg4"], default="auto")
-    ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
+    ap.add_argument("--routing", choices=["zipf", "uniform"], default="uniform",
+                    help="expert-parallel routing (cfg4 lists both; uniform is the balanced case)")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")

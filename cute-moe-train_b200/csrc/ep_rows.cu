@@ -1,0 +1,118 @@
+// Row movement kernels of the expert-parallel MoE FFN (dispatch / combine around the grouped GEMMs).
+//
+//   gather:  dst[i]  = scale[i] * src[idx[i]]                          (scale optional)
+//   combine: out[t]  = sum_j w[t*k + j] * rows[pos[t*k + j]]  for j < k  (fp32 sum, one bf16 rounding)
+//
+// Dispatch is a gather (token copies in expert order), combine sums a token's k expert outputs.
+// Each is the other's backward: d(gather)/d(src) is a combine over the copies of each source row,
+// d(combine)/d(rows) is a gather of the token gradients.  Both are HBM-bound: one warp per row,
+// 16-byte vector loads/stores, a grid of a few waves over the 148 SMs.  The reference has no
+// distributed code; these serve the expert-parallel mode this build adds.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "moe_gemm.h"
+
+namespace mgf {
+namespace {
+
+constexpr int kWarpsPerBlock = 8;
+
+__device__ __forceinline__ float lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t pack(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) gather_rows_kernel(
+    const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ idx,
+    const float* __restrict__ scale, int64_t n_rows, int64_t row_vec, __nv_bfloat16* __restrict__ dst,
+    int64_t ld_dst) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t i = warp0; i < n_rows; i += nwarps) {
+    const int64_t s = __ldg(idx + i);
+    const uint4* sp = reinterpret_cast<const uint4*>(src + s * ld_src);
+    uint4* dp = reinterpret_cast<uint4*>(dst + i * ld_dst);
+    if (scale == nullptr) {
+      for (int64_t v = lane; v < row_vec; v += 32) dp[v] = __ldg(sp + v);
+    } else {
+      const float f = __ldg(scale + i);
+      for (int64_t v = lane; v < row_vec; v += 32) {
+        const uint4 a = __ldg(sp + v);
+        dp[v] = make_uint4(pack(f * lo(a.x), f * hi(a.x)), pack(f * lo(a.y), f * hi(a.y)),
+                           pack(f * lo(a.z), f * hi(a.z)), pack(f * lo(a.w), f * hi(a.w)));
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) combine_rows_kernel(
+    const __nv_bfloat16* __restrict__ rows, int64_t ld_rows, const int64_t* __restrict__ pos,
+    const float* __restrict__ w, int64_t n_out, int k, int64_t row_vec, __nv_bfloat16* __restrict__ out,
+    int64_t ld_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp0; t < n_out; t += nwarps) {
+    uint4* op = reinterpret_cast<uint4*>(out + t * ld_out);
+    for (int64_t v = lane; v < row_vec; v += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < k; ++j) {
+        const int64_t r = __ldg(pos + t * k + j);
+        const float f = (w != nullptr) ? __ldg(w + t * k + j) : 1.0f;
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(rows + r * ld_rows) + v);
+        acc[0] += f * lo(a.x); acc[1] += f * hi(a.x);
+        acc[2] += f * lo(a.y); acc[3] += f * hi(a.y);
+        acc[4] += f * lo(a.z); acc[5] += f * hi(a.z);
+        acc[6] += f * lo(a.w); acc[7] += f * hi(a.w);
+      }
+      op[v] = make_uint4(pack(acc[0], acc[1]), pack(acc[2], acc[3]), pack(acc[4], acc[5]), pack(acc[6], acc[7]));
+    }
+  }
+}
+
+int grid_for(int64_t rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const int64_t cap = static_cast<int64_t>(sms) * 8;  // 8 resident blocks per SM, grid-stride beyond
+  return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace mgf
+
+extern "C" int mgf_gather_rows(const void* src, int64_t ld_src, const int64_t* idx, const float* scale,
+                               int64_t n_rows, int64_t row_elems, void* dst, int64_t ld_dst, void* stream) {
+  using namespace mgf;
+  if (n_rows < 0 || row_elems < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_rows == 0 || row_elems == 0) return MGF_OK;
+  if (src == nullptr || idx == nullptr || dst == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  if (row_elems % 8 || ld_src % 8 || ld_dst % 8 || !aligned16(src) || !aligned16(dst)) return MGF_ERR_ALIGNMENT;
+  gather_rows_kernel<<<grid_for(n_rows), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), ld_src, idx, scale, n_rows, row_elems / 8,
+      static_cast<__nv_bfloat16*>(dst), ld_dst);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t* pos, const float* weights,
+                                int64_t n_out, int32_t k, int64_t row_elems, void* out, int64_t ld_out,
+                                void* stream) {
+  using namespace mgf;
+  if (n_out < 0 || row_elems < 0 || k < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_out == 0 || row_elems == 0) return MGF_OK;
+  if (out == nullptr || (k > 0 && (rows == nullptr || pos == nullptr))) return MGF_ERR_INVALID_ARGUMENT;
+  if (row_elems % 8 || ld_rows % 8 || ld_out % 8 || !aligned16(rows) || !aligned16(out)) return MGF_ERR_ALIGNMENT;
+  combine_rows_kernel<<<grid_for(n_out), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(rows), ld_rows, pos, weights, n_out, k, row_elems / 8,
+      static_cast<__nv_bfloat16*>(out), ld_out);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}

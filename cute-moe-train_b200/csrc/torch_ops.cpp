@@ -300,6 +300,48 @@ std::tuple<Tensor, Tensor> mm_wgrad_bias_cuda(const Tensor& mat_a, const Tensor&
   return ragged_k_launch(mat_a, mat_b, offs, true, "grouped_mm_wgrad_bias");
 }
 
+// ---------------------------------------------------------------- expert-parallel row movement
+void check_rows(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.scalar_type() == at::kBFloat16 && t.stride(1) == 1,
+              name, " must be a row-major 2D bf16 CUDA tensor");
+}
+
+Tensor gather_rows_cuda(const Tensor& src, const Tensor& idx_in, const std::optional<Tensor>& scale_in) {
+  check_rows(src, "src");
+  const c10::cuda::CUDAGuard guard(src.device());
+  Tensor idx = idx_in.to(at::kLong).contiguous();
+  Tensor out = at::empty({idx.numel(), src.size(1)}, src.options());
+  Tensor scale;
+  if (scale_in.has_value()) {
+    scale = scale_in->to(at::kFloat).contiguous();
+    TORCH_CHECK(scale.numel() == idx.numel(), "gather_rows: scale must have one entry per row");
+  }
+  check_launch(mgf_gather_rows(src.data_ptr(), src.stride(0), idx.data_ptr<int64_t>(),
+                               scale.defined() ? scale.data_ptr<float>() : nullptr, idx.numel(), src.size(1),
+                               out.data_ptr(), out.stride(0), at::cuda::getCurrentCUDAStream().stream()),
+               "gather_rows");
+  return out;
+}
+
+Tensor combine_rows_cuda(const Tensor& rows, const Tensor& pos_in, const std::optional<Tensor>& w_in, int64_t k) {
+  check_rows(rows, "rows");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  TORCH_CHECK(k >= 1 && pos_in.numel() % k == 0, "combine_rows: pos must hold k entries per output row");
+  Tensor pos = pos_in.to(at::kLong).contiguous();
+  const int64_t n_out = pos.numel() / k;
+  Tensor out = at::empty({n_out, rows.size(1)}, rows.options());
+  Tensor w;
+  if (w_in.has_value()) {
+    w = w_in->to(at::kFloat).contiguous();
+    TORCH_CHECK(w.numel() == pos.numel(), "combine_rows: one weight per (row, slot)");
+  }
+  check_launch(mgf_combine_rows(rows.data_ptr(), rows.stride(0), pos.data_ptr<int64_t>(),
+                                w.defined() ? w.data_ptr<float>() : nullptr, n_out, static_cast<int32_t>(k),
+                                rows.size(1), out.data_ptr(), out.stride(0), at::cuda::getCurrentCUDAStream().stream()),
+               "combine_rows");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(grouped_mm, m) {
@@ -314,6 +356,8 @@ TORCH_LIBRARY(grouped_mm, m) {
       "mm_downproj(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor aux_biased_acc,"
       " float swiglu_alpha, float swiglu_limit) -> Tensor");
   m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
+  m.def("gather_rows(Tensor src, Tensor idx, Tensor? scale) -> Tensor");
+  m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
@@ -321,6 +365,8 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_swiglu", &mm_swiglu_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
+  m.impl("gather_rows", &gather_rows_cuda);
+  m.impl("combine_rows", &combine_rows_cuda);
   m.impl("mm_downproj",
          [](const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
             const Tensor& aux, double alpha, double limit) {

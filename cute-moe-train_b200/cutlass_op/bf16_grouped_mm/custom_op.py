@@ -330,6 +330,19 @@ torch.library.register_autograd(
     "grouped_mm::mm_downproj", _downproj_backward, setup_context=_downproj_setup_context
 )
 
+# ============================================================================ EP row movement
+
+
+@torch.library.register_fake("grouped_mm::gather_rows")
+def _gather_rows_fake(src, idx, scale):
+    return src.new_empty((idx.numel(), src.shape[1]))
+
+
+@torch.library.register_fake("grouped_mm::combine_rows")
+def _combine_rows_fake(rows, pos, weights, k):
+    return rows.new_empty((pos.numel() // k, rows.shape[1]))
+
+
 # Names the reference module exports (custom_op.py:139, 400, 579): the registered operators.
 grouped_mm_forward = torch.ops.grouped_mm.mm
 grouped_mm_swiglu_forward = torch.ops.grouped_mm.mm_swiglu

@@ -65,6 +65,7 @@ class DispatchPlan:
         # stable sort of the T*k copies by expert id (=> grouped by destination rank as well)
         self.order = torch.argsort(flat, stable=True)
         self.copy_token = torch.div(self.order, k, rounding_mode="floor")
+        self.inv_order = _inverse(self.order)                             # copy (t*k + j) -> sorted position
         counts_e = torch.bincount(flat, minlength=num_experts)            # [E] copies per expert
         send_counts = counts_e.view(world, e_local)                       # [dest rank, local expert]
         recv_counts = torch.empty_like(send_counts)
@@ -84,9 +85,87 @@ class DispatchPlan:
                    + torch.arange(world, device=device).unsqueeze(1))     # [src, expert] -> e*world + src
         row_key = torch.repeat_interleave(seg_key.reshape(-1), recv_counts.reshape(-1), output_size=n_recv)
         self.to_expert_order = torch.argsort(row_key, stable=True)        # expert-ordered row -> received row
+        self.from_expert_order = _inverse(self.to_expert_order)
+        self.identity_order = world == 1                                  # received order is expert order
         per_expert = recv_counts.sum(0)                                   # [local expert]
         self.offs = torch.cumsum(per_expert, 0).to(torch.int32)
         self.local_rows = n_recv
+
+
+def _inverse(perm: torch.Tensor) -> torch.Tensor:
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(perm.numel(), device=perm.device, dtype=perm.dtype)
+    return inv
+
+
+# Row movement.  CUDA tensors go through the grouped_mm::gather_rows / combine_rows kernels (one
+# HBM pass each, fp32 accumulation in the combine); the torch expressions below serve CPU tensors,
+# i.e. the process-group tests of the routing logic that run on CPU ranks.
+def _gather(src, idx, scale=None):
+    if src.is_cuda:
+        return torch.ops.grouped_mm.gather_rows(src, idx, scale)
+    out = src[idx]
+    return out if scale is None else (out.float() * scale.float().unsqueeze(1)).to(src.dtype)
+
+
+def _combine(rows, pos, weights, k):
+    if rows.is_cuda:
+        return torch.ops.grouped_mm.combine_rows(rows, pos, weights, k)
+    g = rows[pos].float().view(-1, k, rows.shape[1])
+    if weights is not None:
+        g = g * weights.float().view(-1, k, 1)
+    return g.sum(1).to(rows.dtype)
+
+
+class _Dispatch(torch.autograd.Function):
+    """Token copies in sorted-by-expert order: out[p] = x[copy_token[p]]."""
+
+    @staticmethod
+    def forward(ctx, x, copy_token, inv_order, k):
+        ctx.save_for_backward(inv_order)
+        ctx.k = k
+        return _gather(x, copy_token)
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv_order,) = ctx.saved_tensors
+        return _combine(g.contiguous(), inv_order, None, ctx.k), None, None, None
+
+
+class _Permute(torch.autograd.Function):
+    """out[i] = x[perm[i]] for a permutation; the gradient moves back with the inverse."""
+
+    @staticmethod
+    def forward(ctx, x, perm, inv_perm):
+        ctx.save_for_backward(inv_perm)
+        return _gather(x, perm)
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv_perm,) = ctx.saved_tensors
+        return _gather(g.contiguous(), inv_perm), None, None
+
+
+class _Combine(torch.autograd.Function):
+    """out[t] = sum_j w[t, j] * ret[inv_order[t*k + j]] (w = 1 when absent), fp32 accumulation."""
+
+    @staticmethod
+    def forward(ctx, ret, inv_order, copy_token, order, w_flat, k):
+        ctx.save_for_backward(ret, inv_order, copy_token, order, w_flat if w_flat is not None else ret.new_empty(0))
+        ctx.k, ctx.has_w = k, w_flat is not None
+        return _combine(ret, inv_order, w_flat, k)
+
+    @staticmethod
+    def backward(ctx, g):
+        ret, inv_order, copy_token, order, w_flat = ctx.saved_tensors
+        g = g.contiguous()
+        scale = w_flat[order] if ctx.has_w else None
+        grad_ret = _gather(g, copy_token, scale)
+        grad_w = None
+        if ctx.has_w and ctx.needs_input_grad[4]:
+            copies = ret[inv_order].float().view(-1, ctx.k, ret.shape[1])
+            grad_w = (copies * g.float().unsqueeze(1)).sum(-1).reshape(-1)
+        return grad_ret, None, None, None, grad_w, None
 
 
 def _all_to_all(x: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
@@ -107,19 +186,16 @@ def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expe
         raise RuntimeError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
     if plan is None:
         plan = DispatchPlan(expert_idx, num_experts, world, group)
-    send = x[plan.copy_token]                                             # [T*k, H] sorted by expert
+    k = plan.topk
+    send = _Dispatch.apply(x, plan.copy_token, plan.inv_order, k)        # [T*k, H] sorted by expert
     recv = _all_to_all(send, plan.recv_splits, plan.send_splits, group) if world > 1 else send
-    rows = recv[plan.to_expert_order]
+    rows = recv if plan.identity_order else _Permute.apply(recv, plan.to_expert_order, plan.from_expert_order)
     y = expert_fn(rows, plan.offs)
-    back = torch.empty_like(y)
-    back = back.index_copy(0, plan.to_expert_order, y)                    # expert order -> received order
+    back = y if plan.identity_order else _Permute.apply(y, plan.from_expert_order, plan.to_expert_order)
     ret = _all_to_all(back, plan.send_splits, plan.recv_splits, group) if world > 1 else back
-    if router_weights is not None:
-        w = router_weights.reshape(-1)[plan.order].to(ret.dtype).unsqueeze(1)
-        ret = ret * w
-    # sum the k copies of every token in fp32, round once
-    out = torch.zeros(x.shape, dtype=torch.float32, device=x.device).index_add(0, plan.copy_token, ret.float())
-    return out.to(x.dtype), plan
+    w_flat = router_weights.reshape(-1).float() if router_weights is not None else None
+    out = _Combine.apply(ret, plan.inv_order, plan.copy_token, plan.order, w_flat, k)
+    return out, plan
 
 
 class EPMoEFFN(torch.nn.Module):

@@ -121,6 +121,18 @@ int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream);
  * nothing (no cudaMalloc/cudaFree).  Same return codes as mgf_grouped_gemm_launch. */
 int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* stream);
 
+/* Expert-parallel row movement (no counterpart in the reference, which has no distributed code).
+ * bf16 rows of row_elems elements (a multiple of 8), row strides ld_* in elements (multiples of 8),
+ * 16-byte aligned bases, int64 device index arrays, optional fp32 device scales (NULL = 1).
+ *   mgf_gather_rows:  dst[i] = scale[i] * src[idx[i]],                     i < n_rows
+ *   mgf_combine_rows: out[t] = sum_{j<k} weights[t*k+j] * rows[pos[t*k+j]], t < n_out (fp32 sum)
+ * Dispatch gathers token copies into expert order; combine sums each token's k expert outputs;
+ * each is the other's backward. */
+int mgf_gather_rows(const void* src, int64_t ld_src, const int64_t* idx, const float* scale, int64_t n_rows,
+                    int64_t row_elems, void* dst, int64_t ld_dst, void* stream);
+int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t* pos, const float* weights, int64_t n_out,
+                     int32_t k, int64_t row_elems, void* out, int64_t ld_out, void* stream);
+
 /* Read (and optionally clear) the device status word of `device`.  Synchronises that
  * device; meant for tests and debugging, never called on the hot path. */
 int mgf_device_status(int device, uint32_t* status_out, int clear);

@@ -89,7 +89,7 @@ def _ep_worker_body(rank, world, port, q):
             parts = [torch.empty_like(w) for _ in range(world)]
             dist.all_gather(parts, w)
             gathered.append(torch.cat(parts, 0).cpu().float().numpy())
-        q.put((rank, x.float().numpy(), idx.numpy(), out.float().cpu().numpy(), gathered))
+        q.put((rank, x.float().numpy(), idx.numpy(), out.detach().float().cpu().numpy(), gathered))
     finally:
         dist.destroy_process_group()
 
@@ -122,4 +122,44 @@ def test_ep_world2_nccl_matches_oracle():
         wts = [torch.from_numpy(w).to(torch.bfloat16) for w in ws]
         ref = _reference_ffn(torch.from_numpy(x).to(torch.bfloat16), torch.from_numpy(idx), *wts)
         r = O.check(f"ep_out_rank{rank}", torch.from_numpy(out), ref)
+        assert r["ok"], r
+
+
+def test_row_kernels_match_torch():
+    """gather_rows / combine_rows against torch indexing, with and without scales."""
+    g = torch.Generator().manual_seed(3)
+    src = torch.randn(50, 264, generator=g).to(torch.bfloat16).cuda()
+    idx = torch.randint(0, 50, (77,), generator=g).cuda()
+    sc = torch.rand(77, generator=g).cuda()
+    assert torch.equal(torch.ops.grouped_mm.gather_rows(src, idx, None), src[idx])
+    ref = (src[idx].float() * sc.unsqueeze(1)).to(torch.bfloat16)
+    assert torch.allclose(torch.ops.grouped_mm.gather_rows(src, idx, sc).float(), ref.float(), rtol=1e-2, atol=1e-2)
+    k = 3
+    pos = torch.randint(0, 50, (20 * k,), generator=g).cuda()
+    w = torch.rand(20 * k, generator=g).cuda()
+    out = torch.ops.grouped_mm.combine_rows(src, pos, w, k)
+    ref = (src[pos].float() * w.unsqueeze(1)).view(20, k, -1).sum(1)
+    r = O.check("combine", out.float().cpu(), ref.cpu())
+    assert r["ok"], r
+
+
+def test_ep_autograd_row_functions():
+    """Gradients of dispatch / permute / combine through the kernels equal torch autograd's."""
+    from cutlass_op.bf16_grouped_mm.expert_parallel import DispatchPlan, _Combine, _Dispatch, route_tokens
+
+    idx = route_tokens(40, 6, 3, "zipf", seed=9).cuda()
+    plan = DispatchPlan(idx, 6, 1)
+    x = torch.randn(40, 64, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = torch.rand(40, 3, generator=torch.Generator().manual_seed(5)).cuda().requires_grad_(True)
+    send = _Dispatch.apply(x, plan.copy_token, plan.inv_order, 3)
+    y = send * 2
+    out = _Combine.apply(y, plan.inv_order, plan.copy_token, plan.order, w.reshape(-1), 3)
+    go = torch.randn(40, 64, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).cuda()
+    out.backward(go)
+    x2 = x.detach().float().requires_grad_(True)
+    w2 = w.detach().requires_grad_(True)
+    ref = (2 * x2.unsqueeze(1) * w2.unsqueeze(2)).sum(1)
+    ref.backward(go.float())
+    for name, a, b in (("out", out, ref), ("dx", x.grad, x2.grad), ("dw", w.grad, w2.grad)):
+        r = O.check(name, a.float().cpu(), b.detach().cpu())
         assert r["ok"], r
