@@ -28,7 +28,8 @@ from typing import Callable
 
 import torch
 import torch.distributed as dist
-import torch.distributed.nn.functional as dist_fn
+
+from .optimer import timed
 
 
 def route_tokens(tokens: int, num_experts: int, topk: int, routing: str = "zipf", seed: int = 0,
@@ -124,12 +125,14 @@ class _Dispatch(torch.autograd.Function):
     def forward(ctx, x, copy_token, inv_order, k):
         ctx.save_for_backward(inv_order)
         ctx.k = k
-        return _gather(x, copy_token)
+        with timed("ep_dispatch_gather"):
+            return _gather(x, copy_token)
 
     @staticmethod
     def backward(ctx, g):
         (inv_order,) = ctx.saved_tensors
-        return _combine(g.contiguous(), inv_order, None, ctx.k), None, None, None
+        with timed("ep_dispatch_gather_bwd"):
+            return _combine(g.contiguous(), inv_order, None, ctx.k), None, None, None
 
 
 class _Permute(torch.autograd.Function):
@@ -138,12 +141,14 @@ class _Permute(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, perm, inv_perm):
         ctx.save_for_backward(inv_perm)
-        return _gather(x, perm)
+        with timed("ep_permute"):
+            return _gather(x, perm)
 
     @staticmethod
     def backward(ctx, g):
         (inv_perm,) = ctx.saved_tensors
-        return _gather(g.contiguous(), inv_perm), None, None
+        with timed("ep_permute_bwd"):
+            return _gather(g.contiguous(), inv_perm), None, None
 
 
 class _Combine(torch.autograd.Function):
@@ -153,14 +158,16 @@ class _Combine(torch.autograd.Function):
     def forward(ctx, ret, inv_order, copy_token, order, w_flat, k):
         ctx.save_for_backward(ret, inv_order, copy_token, order, w_flat if w_flat is not None else ret.new_empty(0))
         ctx.k, ctx.has_w = k, w_flat is not None
-        return _combine(ret, inv_order, w_flat, k)
+        with timed("ep_combine"):
+            return _combine(ret, inv_order, w_flat, k)
 
     @staticmethod
     def backward(ctx, g):
         ret, inv_order, copy_token, order, w_flat = ctx.saved_tensors
         g = g.contiguous()
         scale = w_flat[order] if ctx.has_w else None
-        grad_ret = _gather(g, copy_token, scale)
+        with timed("ep_combine_bwd"):
+            grad_ret = _gather(g, copy_token, scale)
         grad_w = None
         if ctx.has_w and ctx.needs_input_grad[4]:
             copies = ret[inv_order].float().view(-1, ctx.k, ret.shape[1])
@@ -168,9 +175,28 @@ class _Combine(torch.autograd.Function):
         return grad_ret, None, None, None, grad_w, None
 
 
-def _all_to_all(x: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
+def _exchange(x: torch.Tensor, out_splits, in_splits, group, name) -> torch.Tensor:
     out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
-    return dist_fn.all_to_all_single(out, x.contiguous(), out_splits, in_splits, group=group)
+    with timed(name):
+        dist.all_to_all_single(out, x.contiguous(), out_splits, in_splits, group=group)
+    return out
+
+
+class _AllToAll(torch.autograd.Function):
+    """Uneven all-to-all of rows; its gradient is the same exchange with the splits swapped."""
+
+    @staticmethod
+    def forward(ctx, x, out_splits, in_splits, group):
+        ctx.out_splits, ctx.in_splits, ctx.group = out_splits, in_splits, group
+        return _exchange(x, out_splits, in_splits, group, "ep_all_to_all")
+
+    @staticmethod
+    def backward(ctx, g):
+        return _exchange(g, ctx.in_splits, ctx.out_splits, ctx.group, "ep_all_to_all_bwd"), None, None, None
+
+
+def _all_to_all(x: torch.Tensor, out_splits, in_splits, group) -> torch.Tensor:
+    return _AllToAll.apply(x, out_splits, in_splits, group)
 
 
 def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
@@ -185,7 +211,8 @@ def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expe
     if num_experts % world:
         raise RuntimeError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
     if plan is None:
-        plan = DispatchPlan(expert_idx, num_experts, world, group)
+        with timed("ep_plan"):
+            plan = DispatchPlan(expert_idx, num_experts, world, group)
     k = plan.topk
     send = _Dispatch.apply(x, plan.copy_token, plan.inv_order, k)        # [T*k, H] sorted by expert
     recv = _all_to_all(send, plan.recv_splits, plan.send_splits, group) if world > 1 else send
