@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["auto", "cfg3", "cfg4"], default="auto")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="uniform",
                     help="expert-parallel routing (cfg4 lists both; uniform is the balanced case)")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -154,7 +156,8 @@ def build_workload(args, rank, world, device):
         E_total = args.experts or 128
         zero = 0
         desc = (f"cfg4: GPT-OSS-120B experts E=128 H=I=2880, 24576 tokens/rank top-4 {args.routing} routing, "
-                f"expert parallel E/{world} per GPU, NCCL all-to-all dispatch/combine")
+                f"expert parallel E/{world} per GPU, dispatch/combine by "
+                + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all"))
     return wl, desc, E_total, zero, tokens, topk, H, I
 
 
@@ -291,7 +294,7 @@ def main():
     else:
         from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
-        ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2)
+        ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport)
         gx = torch.Generator(device=device).manual_seed(1 + rank)
         x = torch.randn(tokens, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
         expert_idx = route_tokens(tokens, E_total, topk, args.routing, seed=100 + rank, device=device)
@@ -321,7 +324,7 @@ def main():
         clocks = sampler.stop()
     ops = timer.summary()
     if world > 1:
-        local_rows = ffn.last_local_rows
+        local_rows = int(ffn.last_local_rows)
     flops_local = 18.0 * local_rows * H * I
     t = torch.tensor([ms, flops_local], dtype=torch.float64, device=device)
     if world > 1:

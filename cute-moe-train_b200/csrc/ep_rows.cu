@@ -76,6 +76,46 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) combine_rows_kernel(
   }
 }
 
+// Rows written straight into other GPUs' memory (NVLink peer stores through CUDA IPC mappings):
+// dst_rank[i]'s buffer (peer_bases[dst_rank[i]]) row dst_row[i] = scale[i] * src[src_idx[i]].
+// The row count is n_max, or *n_dev when given (a device-side count, never read by the host).
+__global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
+    const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ src_idx,
+    const float* __restrict__ scale, int64_t n_max, const int32_t* __restrict__ n_dev,
+    const int64_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
+    const unsigned long long* __restrict__ peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
+    int64_t row_vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  int64_t n = n_max;
+  if (n_dev != nullptr) {
+    const int64_t c = __ldg(n_dev);
+    n = c < n ? (c > 0 ? c : 0) : n;
+  }
+  for (int64_t i = warp0; i < n; i += nwarps) {
+    const int64_t s = src_idx != nullptr ? __ldg(src_idx + i) : i;
+    const int64_t r = __ldg(dst_rank + i);
+    const int64_t row = __ldg(dst_row + i);
+    if (r < 0 || r >= world || row < 0 || row >= dst_rows) continue;  // never store outside a peer buffer
+    __nv_bfloat16* dbase = reinterpret_cast<__nv_bfloat16*>(peer_bases[r]);
+    const uint4* sp = reinterpret_cast<const uint4*>(src + s * ld_src);
+    uint4* dp = reinterpret_cast<uint4*>(dbase + row * ld_dst);
+    if (scale == nullptr) {
+      for (int64_t v = lane; v < row_vec; v += 32) dp[v] = __ldg(sp + v);
+    } else {
+      const float f = __ldg(scale + i);
+      for (int64_t v = lane; v < row_vec; v += 32) {
+        const uint4 a = __ldg(sp + v);
+        dp[v] = make_uint4(pack(f * lo(a.x), f * hi(a.x)), pack(f * lo(a.y), f * hi(a.y)),
+                           pack(f * lo(a.z), f * hi(a.z)), pack(f * lo(a.w), f * hi(a.w)));
+      }
+    }
+  }
+  // make the peer stores visible system-wide before the stream's next (barrier) operation
+  __threadfence_system();
+}
+
 int grid_for(int64_t rows) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -114,5 +154,21 @@ extern "C" int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t
   combine_rows_kernel<<<grid_for(n_out), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(rows), ld_rows, pos, weights, n_out, k, row_elems / 8,
       static_cast<__nv_bfloat16*>(out), ld_out);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src_idx, const float* scale,
+                             int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
+                             const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
+                             int64_t row_elems, void* stream) {
+  using namespace mgf;
+  if (n_max < 0 || row_elems < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_max == 0 || row_elems == 0) return MGF_OK;
+  if (src == nullptr || dst_rank == nullptr || dst_row == nullptr || peer_bases == nullptr)
+    return MGF_ERR_INVALID_ARGUMENT;
+  if (row_elems % 8 || ld_src % 8 || ld_dst % 8 || !aligned16(src)) return MGF_ERR_ALIGNMENT;
+  push_rows_kernel<<<grid_for(n_max), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), ld_src, src_idx, scale, n_max, n_dev, dst_rank, dst_row, peer_bases,
+      world, dst_rows, ld_dst, row_elems / 8);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }

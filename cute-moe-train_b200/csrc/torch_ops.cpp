@@ -342,6 +342,42 @@ Tensor combine_rows_cuda(const Tensor& rows, const Tensor& pos_in, const std::op
   return out;
 }
 
+// Rows of src pushed into other ranks' IPC-mapped buffers (see mgf_push_rows).
+void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, const std::optional<Tensor>& scale,
+                    const std::optional<Tensor>& n_dev, const Tensor& dst_rank, const Tensor& dst_row,
+                    const Tensor& peer_bases, int64_t dst_rows, int64_t ld_dst, int64_t n_max) {
+  check_rows(src, "src");
+  const c10::cuda::CUDAGuard guard(src.device());
+  TORCH_CHECK(dst_rank.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong &&
+                  peer_bases.scalar_type() == at::kLong && dst_rank.is_contiguous() && dst_row.is_contiguous() &&
+                  peer_bases.is_contiguous(),
+              "push_rows: dst_rank, dst_row and peer_bases must be contiguous int64");
+  TORCH_CHECK(dst_rank.numel() >= n_max && dst_row.numel() >= n_max, "push_rows: index arrays shorter than n_max");
+  const int64_t* si = nullptr;
+  if (src_idx.has_value()) {
+    TORCH_CHECK(src_idx->scalar_type() == at::kLong && src_idx->is_contiguous() && src_idx->numel() >= n_max,
+                "push_rows: src_idx must be contiguous int64 with n_max entries");
+    si = src_idx->data_ptr<int64_t>();
+  }
+  const float* sc = nullptr;
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() && scale->numel() >= n_max,
+                "push_rows: scale must be contiguous float32 with n_max entries");
+    sc = scale->data_ptr<float>();
+  }
+  const int32_t* nd = nullptr;
+  if (n_dev.has_value()) {
+    TORCH_CHECK(n_dev->scalar_type() == at::kInt && n_dev->numel() >= 1, "push_rows: n_dev must be int32");
+    nd = n_dev->data_ptr<int32_t>();
+  }
+  check_launch(mgf_push_rows(src.data_ptr(), src.stride(0), si, sc, n_max, nd, dst_rank.data_ptr<int64_t>(),
+                             dst_row.data_ptr<int64_t>(),
+                             reinterpret_cast<const unsigned long long*>(peer_bases.data_ptr<int64_t>()),
+                             peer_bases.numel(), dst_rows, ld_dst, src.size(1),
+                             at::cuda::getCurrentCUDAStream().stream()),
+               "push_rows");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(grouped_mm, m) {
@@ -358,6 +394,9 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
   m.def("gather_rows(Tensor src, Tensor idx, Tensor? scale) -> Tensor");
   m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
+  m.def(
+      "push_rows(Tensor src, Tensor? src_idx, Tensor? scale, Tensor? n_dev, Tensor dst_rank, Tensor dst_row,"
+      " Tensor peer_bases, int dst_rows, int ld_dst, int n_max) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
@@ -367,6 +406,7 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
   m.impl("gather_rows", &gather_rows_cuda);
   m.impl("combine_rows", &combine_rows_cuda);
+  m.impl("push_rows", &push_rows_cuda);
   m.impl("mm_downproj",
          [](const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
             const Tensor& aux, double alpha, double limit) {

@@ -225,12 +225,203 @@ def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expe
     return out, plan
 
 
+# ============================================================================ peer-memory transport
+#
+# The NCCL path above moves every row three times per direction (gather into a send buffer, the
+# all-to-all, a permutation into expert order).  The peer path writes each row once, straight into
+# its final place in another GPU's memory: every rank owns four receive buffers, shared with all
+# ranks of the group through CUDA IPC once (no multicast object):
+#   rows  [cap, H]   expert-ordered token rows of this rank's experts   (forward dispatch target)
+#   ret   [T*k, H]   expert outputs of this rank's token copies, sorted (forward combine target)
+#   grows [cap, H]   gradients of `rows`                                 (backward of the combine)
+#   gret  [T*k, H]   gradients of this rank's token copies               (backward of the dispatch)
+# cap = T*k*world, the most rows one rank can receive.  All destination rows are computed on the
+# device from the all-gathered (source rank, expert) count matrix, so no split size is read on the
+# host.  A stream-ordered NCCL all-reduce of one element separates the writers from the readers.
+
+
+def push_plan(c_all: torch.Tensor, e_sorted: torch.Tensor, rank: int, world: int, e_local: int, cap: int) -> dict:
+    """Destination and source maps of the peer transport, on the device (no host synchronisation).
+
+    c_all: [world, E] copies from source rank s to expert e; e_sorted: this rank's copy experts in
+    sorted order.  Returns
+      dst_rank/dst_row [T*k]: where sorted copy p of this rank lands (owner rank, row of its `rows`);
+      src_rank/src_pos [cap]: for row j of this rank's `rows`, the source rank and its sorted copy;
+      offs [e_local] int32 and n_recv [1] int32 of the received rows.
+    Owner row layout: local expert-major, source rank next, the source's copies in sorted order.
+    """
+    dev = c_all.device
+    E = c_all.shape[1]
+    n = e_sorted.numel()
+    ex = lambda t, d: t.cumsum(d) - t  # noqa: E731  exclusive cumulative sum
+    pos = ex(c_all, 1)                                           # [world, E] first sorted copy per expert
+    tot = c_all.sum(0)                                           # [E] rows of each expert
+    base = ex(tot.view(world, e_local), 1).reshape(E)            # expert's first row within its owner
+    before = ex(c_all, 0)                                        # [world, E] rows from lower source ranks
+    within = torch.arange(n, device=dev) - pos[rank][e_sorted]
+    dst_row = base[e_sorted] + before[rank][e_sorted] + within
+    dst_rank = torch.div(e_sorted, e_local, rounding_mode="floor")
+    cl = c_all[:, rank * e_local:(rank + 1) * e_local]          # [world, e_local]
+    seg = cl.t().reshape(-1)                                     # (local expert, source) segments
+    seg_end = seg.cumsum(0)
+    seg_start = seg_end - seg
+    j = torch.arange(cap, device=dev)
+    sid = torch.searchsorted(seg_end, j, right=True).clamp_(max=seg.numel() - 1)
+    e_l = torch.div(sid, world, rounding_mode="floor")
+    src = sid - e_l * world
+    src_pos = pos[src, rank * e_local + e_l] + (j - seg_start[sid])
+    offs = cl.sum(0).cumsum(0).to(torch.int32)
+    return {"dst_rank": dst_rank.contiguous(), "dst_row": dst_row.contiguous(), "src_rank": src.contiguous(),
+            "src_pos": src_pos.contiguous(), "offs": offs, "n_recv": offs[-1:].contiguous()}
+
+
+class PeerBuffers:
+    """Receive buffers shared with every rank of `group` through CUDA IPC (allocated once)."""
+
+    def __init__(self, shapes: dict, dtype, device, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.local = {k: torch.empty(v, dtype=dtype, device=device) for k, v in shapes.items()}
+        handles = {k: t.untyped_storage()._share_cuda_() for k, t in self.local.items()}
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        self._opened = []
+        self.bases = {}
+        for k, t in self.local.items():
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(t.data_ptr())
+                else:
+                    st = torch.UntypedStorage._new_shared_cuda(*everyone[r][k])
+                    self._opened.append(st)
+                    ptrs.append(st.data_ptr())
+            self.bases[k] = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def barrier(self):
+        """Stream-ordered: work queued after it starts only once every rank's earlier work is done."""
+        with timed("ep_peer_barrier"):
+            dist.all_reduce(self._flag, group=self.group)
+
+
+class _PeerState:
+    pass
+
+
+class _PeerDispatch(torch.autograd.Function):
+    """x [T, H] -> this rank's expert-ordered rows [cap, H], rows written by their source ranks."""
+
+    @staticmethod
+    def forward(ctx, x, st):
+        ctx.st = st
+        with timed("ep_peer_dispatch"):
+            torch.ops.grouped_mm.push_rows(x.contiguous(), st.copy_token, None, None, st.plan["dst_rank"],
+                                           st.plan["dst_row"], st.bufs.bases["rows"], st.cap, x.shape[1], st.n)
+        st.bufs.barrier()
+        return st.bufs.local["rows"].view(st.cap, x.shape[1])
+
+    @staticmethod
+    def backward(ctx, g_rows):
+        st = ctx.st
+        with timed("ep_peer_dispatch_bwd"):
+            torch.ops.grouped_mm.push_rows(g_rows.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
+                                           st.plan["src_pos"], st.bufs.bases["gret"], st.n, g_rows.shape[1], st.cap)
+        st.bufs.barrier()
+        with timed("ep_combine"):
+            gx = torch.ops.grouped_mm.combine_rows(st.bufs.local["gret"], st.inv_order, None, st.k)
+        return gx, None
+
+
+class _PeerCombine(torch.autograd.Function):
+    """Expert outputs [cap, H] -> per-token sums [T, H]; rows written back into their sources."""
+
+    @staticmethod
+    def forward(ctx, y, w_flat, st):
+        ctx.st, ctx.has_w = st, w_flat is not None
+        ctx.save_for_backward(w_flat if w_flat is not None else y.new_empty(0))
+        with timed("ep_peer_combine"):
+            torch.ops.grouped_mm.push_rows(y.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
+                                           st.plan["src_pos"], st.bufs.bases["ret"], st.n, y.shape[1], st.cap)
+        st.bufs.barrier()
+        with timed("ep_combine"):
+            return torch.ops.grouped_mm.combine_rows(st.bufs.local["ret"], st.inv_order, w_flat, st.k)
+
+    @staticmethod
+    def backward(ctx, g):
+        st = ctx.st
+        (w_flat,) = ctx.saved_tensors
+        g = g.contiguous()
+        scale = w_flat[st.order].contiguous() if ctx.has_w else None
+        with timed("ep_peer_combine_bwd"):
+            torch.ops.grouped_mm.push_rows(g, st.copy_token, scale, None, st.plan["dst_rank"], st.plan["dst_row"],
+                                           st.bufs.bases["grows"], st.cap, g.shape[1], st.n)
+        st.bufs.barrier()
+        grad_w = None
+        if ctx.has_w and ctx.needs_input_grad[1]:
+            copies = st.bufs.local["ret"][st.inv_order].float().view(-1, st.k, g.shape[1])
+            grad_w = (copies * g.float().unsqueeze(1)).sum(-1).reshape(-1)
+        return st.bufs.local["grows"].view(st.cap, g.shape[1]), grad_w, None
+
+
+def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
+                    bufs_cache: dict, group=None, router_weights: torch.Tensor | None = None) -> tuple:
+    """Expert-parallel MoE FFN with dispatch/combine as peer-memory pushes (CUDA, world > 1).
+
+    Same contract as ep_moe_ffn.  Every rank must pass the same number of tokens.  The receive buffers
+    of one call stay live until its backward ran; a second forward before that backward raises.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if num_experts % world:
+        raise RuntimeError(f"num_experts ({num_experts}) must be divisible by the world size ({world})")
+    T, H = x.shape
+    k = expert_idx.shape[1]
+    e_local = num_experts // world
+    n, cap = T * k, T * k * world
+    key = (n, H, x.dtype)
+    bufs = bufs_cache.get(key)
+    if bufs is None:
+        bufs = PeerBuffers({"rows": (cap, H), "grows": (cap, H), "ret": (n, H), "gret": (n, H)}, x.dtype, x.device,
+                           group)
+        bufs_cache.clear()
+        bufs_cache[key] = bufs
+    if getattr(bufs, "pending_backward", False) and torch.is_grad_enabled():
+        raise RuntimeError("ep_moe_ffn_peer: a second forward before the previous one's backward would overwrite "
+                           "its receive buffers")
+    st = _PeerState()
+    with timed("ep_plan"):
+        flat = expert_idx.reshape(-1).to(torch.int64)
+        st.order = torch.argsort(flat, stable=True)
+        st.copy_token = torch.div(st.order, k, rounding_mode="floor").contiguous()
+        st.inv_order = _inverse(st.order)
+        counts = torch.bincount(flat, minlength=num_experts)
+        c_all = torch.empty(world, num_experts, dtype=counts.dtype, device=x.device)
+        # the count exchange also orders this call after every rank's previous use of the buffers
+        dist.all_gather_into_tensor(c_all, counts, group=group)
+        st.plan = push_plan(c_all, flat[st.order], rank, world, e_local, cap)
+    st.bufs, st.k, st.n, st.cap = bufs, k, n, cap
+    rows = _PeerDispatch.apply(x, st)
+    y = expert_fn(rows, st.plan["offs"])
+    w_flat = router_weights.reshape(-1).float().contiguous() if router_weights is not None else None
+    out = _PeerCombine.apply(y, w_flat, st)
+    bufs.pending_backward = out.requires_grad
+    if out.requires_grad:
+        out.register_hook(lambda g: (setattr(bufs, "pending_backward", False), g)[1])
+    return out, st
+
+
 class EPMoEFFN(torch.nn.Module):
     """GPT-OSS-style MoE FFN whose E experts are sharded E/N per rank, run with the fused kernels."""
 
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
-                 swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0):
+                 swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer"):
         super().__init__()
+        if transport not in ("peer", "nccl"):
+            raise ValueError(f"transport must be 'peer' or 'nccl', got {transport!r}")
+        self.transport = transport
+        self._peer_bufs: dict = {}
         from .workloads import MoEShape, make_weights_device
 
         world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -255,6 +446,12 @@ class EPMoEFFN(torch.nn.Module):
         return grouped_mm_downproj(s, self.w_down, offs, self.b_down, aux, self.alpha, self.limit)
 
     def forward(self, x: torch.Tensor, expert_idx: torch.Tensor, router_weights: torch.Tensor | None = None):
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        if self.transport == "peer" and world > 1 and x.is_cuda:
+            out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self.expert_fn, self._peer_bufs, self.group,
+                                      router_weights)
+            self.last_local_rows = st.plan["n_recv"]  # device tensor; read it outside timed regions
+            return out
         out, plan = ep_moe_ffn(x, expert_idx, self.num_experts, self.expert_fn, self.group, router_weights)
         self.last_local_rows = plan.local_rows
         return out

@@ -133,6 +133,18 @@ int mgf_gather_rows(const void* src, int64_t ld_src, const int64_t* idx, const f
 int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t* pos, const float* weights, int64_t n_out,
                      int32_t k, int64_t row_elems, void* out, int64_t ld_out, void* stream);
 
+/* Expert-parallel push over NVLink peer memory (no counterpart in the reference): for i < n rows
+ * (n = n_max, or *n_dev when n_dev is non-NULL -- a device-side count), write
+ * scale[i] * src[src_idx[i]] (src_idx NULL = i, scale NULL = 1) to row dst_row[i] of the buffer at
+ * peer_bases[dst_rank[i]] (device array of `world` base addresses, one per rank, from CUDA IPC
+ * mappings; each buffer dst_rows rows of stride ld_dst).  Rows whose rank or destination row falls
+ * outside [0, world) x [0, dst_rows) are skipped.  Plain peer stores, no multicast; the caller
+ * orders them before the readers with a stream-ordered barrier. */
+int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src_idx, const float* scale, int64_t n_max,
+                  const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
+                  const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
+                  int64_t row_elems, void* stream);
+
 /* Read (and optionally clear) the device status word of `device`.  Synchronises that
  * device; meant for tests and debugging, never called on the hot path. */
 int mgf_device_status(int device, uint32_t* status_out, int clear);

@@ -166,3 +166,41 @@ def test_world1_identity_experts_sum_copies():
     out, plan = ep_moe_ffn(x, idx, 3, lambda r, o: r)
     assert torch.allclose(out, 2 * x)
     assert plan.offs.tolist() == [4, 7, 10]
+
+
+@pytest.mark.parametrize("world,E,T,K", [(2, 8, 24, 2), (4, 8, 50, 3), (3, 6, 7, 2)])
+def test_push_plan_is_a_consistent_exchange(world, E, T, K):
+    """Simulate every rank of the peer transport in one process: the destination map (source side) and
+    the source map (owner side) are inverse to each other, rows land expert-major then source-major,
+    and the owner's offs count exactly the rows it receives."""
+    from cutlass_op.bf16_grouped_mm.expert_parallel import push_plan, route_tokens
+
+    el = E // world
+    idx = [route_tokens(T, E, K, "zipf" if r % 2 else "uniform", seed=10 + r) for r in range(world)]
+    flats = [i.reshape(-1) for i in idx]
+    orders = [torch.argsort(f, stable=True) for f in flats]
+    c_all = torch.stack([torch.bincount(f, minlength=E) for f in flats])
+    cap = T * K * world
+    plans = [push_plan(c_all, flats[r][orders[r]], r, world, el, cap) for r in range(world)]
+    # push: owner o's row (dst_row) receives (source s, sorted copy p)
+    received = [dict() for _ in range(world)]
+    for s in range(world):
+        for p in range(T * K):
+            o, row = int(plans[s]["dst_rank"][p]), int(plans[s]["dst_row"][p])
+            assert 0 <= row < cap and (row not in received[o])
+            received[o][row] = (s, p)
+    for o in range(world):
+        n = int(plans[o]["n_recv"][0])
+        assert sorted(received[o]) == list(range(n))
+        assert plans[o]["offs"].tolist() == torch.cumsum(c_all[:, o * el:(o + 1) * el].sum(0), 0).tolist()
+        for row in range(n):
+            s, p = received[o][row]
+            assert int(plans[o]["src_rank"][row]) == s and int(plans[o]["src_pos"][row]) == p
+        # expert-major, then source-major order
+        keys = []
+        for row in range(n):
+            s, p = received[o][row]
+            e = int(flats[s][orders[s][p]])
+            assert e // el == o
+            keys.append((e, s, p))
+        assert keys == sorted(keys)

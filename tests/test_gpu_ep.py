@@ -163,3 +163,70 @@ def test_ep_autograd_row_functions():
     for name, a, b in (("out", out, ref), ("dx", x.grad, x2.grad), ("dw", w.grad, w2.grad)):
         r = O.check(name, a.float().cpu(), b.detach().cpu())
         assert r["ok"], r
+
+
+def _transport_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        from conftest import PKG  # noqa: F401
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        try:
+            from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+            res = {}
+            for transport in ("nccl", "peer"):
+                ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport)
+                x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
+                x = x.to(dev).requires_grad_(True)
+                idx = route_tokens(T, E, K, "zipf", seed=20 + rank).to(dev)
+                w = torch.rand(T, K, generator=torch.Generator().manual_seed(30 + rank)).to(dev)
+                for step in range(2):  # second step reuses the peer buffers
+                    x.grad = None
+                    ffn.zero_grad()
+                    out = ffn(x, idx, w)
+                    g = torch.randn(T, H, generator=torch.Generator().manual_seed(40 + rank + step)).to(torch.bfloat16)
+                    out.backward(g.to(dev))
+                torch.cuda.synchronize()
+                res[transport] = [t.detach().float().cpu().numpy() for t in
+                                  (out, x.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad, ffn.b_down.grad)]
+            q.put((rank, res))
+        finally:
+            dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_world2_peer_transport_matches_nccl():
+    """Dispatch/combine as peer-memory pushes gives the NCCL all-to-all path's outputs and gradients."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_transport_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=300)
+            assert r[1] != "error", r[2]
+            res[r[0]] = r[1]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    names = ["out", "dx", "dw_up", "db_up", "dw_down", "db_down"]
+    for rank in range(2):
+        for name, a, b in zip(names, res[rank]["peer"], res[rank]["nccl"]):
+            r = O.check(f"rank{rank}:{name}", torch.from_numpy(a), torch.from_numpy(b))
+            assert r["ok"], r
