@@ -8,10 +8,12 @@
 // d(combine)/d(rows) is a gather of the token gradients.  Both are HBM-bound: one warp per row,
 // 16-byte vector loads/stores, a grid of a few waves over the 148 SMs.  The reference has no
 // distributed code; these serve the expert-parallel mode this build adds.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "moe_gemm.h"
 
@@ -171,4 +173,48 @@ extern "C" int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src
       static_cast<const __nv_bfloat16*>(src), ld_src, src_idx, scale, n_max, n_dev, dst_rank, dst_row, peer_bases,
       world, dst_rows, ld_dst, row_elems / 8);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+// Export an IPC handle for the allocation holding `ptr`: the 64-byte cudaIpcMemHandle_t of the
+// allocation base and the byte offset of `ptr` inside it (the base is found with the driver's
+// cuMemGetAddressRange, reached through cudaGetDriverEntryPoint).
+extern "C" int mgf_ipc_get_handle(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range_fn = nullptr;
+  if (range_fn == nullptr) {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return MGF_ERR_CUDA;
+    range_fn = reinterpret_cast<RangeFn>(fp);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return MGF_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return MGF_ERR_CUDA;
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return MGF_OK;
+}
+
+// CUDA IPC mapping of another process's device allocation into THIS device's context (the calling
+// thread's current device), with peer access enabled lazily: kernels on this device may then store
+// to the peer allocation over NVLink.  `handle` is the 64-byte cudaIpcMemHandle_t of the peer's
+// allocation base.
+extern "C" int mgf_ipc_open(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MGF_ERR_CUDA;
+  *base_out = p;
+  return MGF_OK;
+}
+
+extern "C" int mgf_ipc_close(void* base) {
+  if (base == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }

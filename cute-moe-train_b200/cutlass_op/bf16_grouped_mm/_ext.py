@@ -39,7 +39,38 @@ lib.mgf_status_string.restype = ctypes.c_char_p
 lib.mgf_status_string.argtypes = [ctypes.c_int]
 lib.mgf_device_status.restype = ctypes.c_int
 lib.mgf_device_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
+lib.mgf_ipc_open.restype = ctypes.c_int
+lib.mgf_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+lib.mgf_ipc_get_handle.restype = ctypes.c_int
+lib.mgf_ipc_get_handle.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+lib.mgf_ipc_close.restype = ctypes.c_int
+lib.mgf_ipc_close.argtypes = [ctypes.c_void_p]
 torch.ops.load_library(str(OPS_PATH))
+
+
+def ipc_handle(ptr: int) -> tuple[bytes, int]:
+    """(64-byte IPC handle of the allocation holding device address `ptr`, ptr's offset in it)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64(0)
+    rc = lib.mgf_ipc_get_handle(ctypes.c_void_p(ptr), buf, ctypes.byref(off))
+    if rc != 0:
+        raise RuntimeError(f"mgf_ipc_get_handle failed: {lib.mgf_status_string(rc).decode()}")
+    return buf.raw, int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's CUDA IPC allocation into the current device's context; returns its base address."""
+    if len(handle) != 64:
+        raise RuntimeError(f"ipc_open: expected a 64-byte cudaIpcMemHandle_t, got {len(handle)} bytes")
+    out = ctypes.c_void_p()
+    rc = lib.mgf_ipc_open(handle, ctypes.byref(out))
+    if rc != 0:
+        raise RuntimeError(f"mgf_ipc_open failed: {lib.mgf_status_string(rc).decode()}")
+    return int(out.value)
+
+
+def ipc_close(base: int) -> None:
+    lib.mgf_ipc_close(ctypes.c_void_p(base))
 
 
 def device_status(device: int | None = None, clear: bool = True) -> int:

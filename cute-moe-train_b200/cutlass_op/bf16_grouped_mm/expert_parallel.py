@@ -283,22 +283,38 @@ class PeerBuffers:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.local = {k: torch.empty(v, dtype=dtype, device=device) for k, v in shapes.items()}
-        handles = {k: t.untyped_storage()._share_cuda_() for k, t in self.local.items()}
+        from ._ext import ipc_handle
+
+        handles = {k: ipc_handle(t.data_ptr()) for k, t in self.local.items()}
         everyone = [None] * self.world
         dist.all_gather_object(everyone, handles, group=group)
-        self._opened = []
+        # Open every peer allocation with THIS rank's device current (mgf_ipc_open), so this device
+        # gets peer access to it; torch's own IPC path would map it into the peer device's context.
+        # Buffers carved from one allocation segment share a handle: open each handle once.
+        from ._ext import ipc_open
+
+        self._opened = {}
         self.bases = {}
         for k, t in self.local.items():
             ptrs = []
             for r in range(self.world):
                 if r == self.rank:
                     ptrs.append(t.data_ptr())
-                else:
-                    st = torch.UntypedStorage._new_shared_cuda(*everyone[r][k])
-                    self._opened.append(st)
-                    ptrs.append(st.data_ptr())
+                    continue
+                handle, offset = everyone[r][k]
+                if handle not in self._opened:
+                    self._opened[handle] = ipc_open(handle)
+                ptrs.append(self._opened[handle] + offset)
             self.bases[k] = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def close(self):
+        from ._ext import ipc_close
+
+        torch.cuda.synchronize()
+        for base in self._opened.values():
+            ipc_close(base)
+        self._opened = {}
 
     def barrier(self):
         """Stream-ordered: work queued after it starts only once every rank's earlier work is done."""

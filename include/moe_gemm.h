@@ -145,6 +145,15 @@ int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src_idx, const
                   const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
                   int64_t row_elems, void* stream);
 
+/* Map a peer process's device allocation (its 64-byte cudaIpcMemHandle_t) into the context of
+ * the calling thread's current device, peer access enabled, for mgf_push_rows destinations
+ * (no counterpart in the reference).  mgf_ipc_close unmaps it. */
+int mgf_ipc_open(const void* handle, void** base_out);
+/* The 64-byte IPC handle of the allocation containing device pointer `ptr`, and ptr's byte offset
+ * in it (what a peer passes to mgf_ipc_open, then adds the offset). */
+int mgf_ipc_get_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+int mgf_ipc_close(void* base);
+
 /* Read (and optionally clear) the device status word of `device`.  Synchronises that
  * device; meant for tests and debugging, never called on the hot path. */
 int mgf_device_status(int device, uint32_t* status_out, int clear);
