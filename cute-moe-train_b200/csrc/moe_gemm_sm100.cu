@@ -86,6 +86,7 @@ struct Params {
   int64_t ld_aux;
   float alpha, limit;
   int store_aux;
+  int stall_test;     // test hook: the producer hands out no tiles, so every consumer wait runs out
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
 };
 
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // launch has one) and hands every tile id to the MMA and epilogue warps through the ring.
       int t = unit;
       uint32_t rslot = 0, rphase = 0;
-      while (ok) {
+      while (ok && !p.stall_test) {
         if (!wait_bounded(ptx::smem_u32(&ring_empty[rslot]), rphase ^ 1, abort_flag)) { ok = false; break; }
         const int tt = t < total_tiles ? t : -1;
         ring_ids[rslot] = tt;
@@ -1115,6 +1116,13 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // The dynamic tile counter serves single CTAs only: both CTAs of a pair must walk the same tile
   // sequence, which static striding gives them.
   p.tile_counter = (g.epilogue == MGF_EPI_WGRAD && cg == 1) ? g.workspace : nullptr;
+  // Test hook for the bounded waits: with MGF_TEST_STALL_PRODUCER=1 the kernel does no work and
+  // every consumer wait gives up after its limit, setting MGF_DEV_WAIT_TIMEOUT.  Nothing is in flight
+  // when they give up, so the context stays usable; tests use it to exercise that path on a GPU.
+  {
+    const char* env = getenv("MGF_TEST_STALL_PRODUCER");
+    p.stall_test = (env != nullptr && env[0] == '1') ? 1 : 0;
+  }
   if (cg == 2) {
     switch (bn) {
       case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
