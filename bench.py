@@ -49,7 +49,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["auto", "cfg3", "cfg4"], default="auto")
+    ap.add_argument("--workload", choices=["auto", "cfg2", "cfg3", "cfg4", "cfg5"], default="auto",
+                    help="cfg3 (1 GPU) / cfg4 (EP) by default; cfg2 = forward only; cfg5 = E=256 fine-grained")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="uniform",
                     help="expert-parallel routing (cfg4 lists both; uniform is the balanced case)")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
@@ -57,7 +58,8 @@ def parse_args():
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--tokens", type=int, default=24576, help="tokens per GPU (smaller for profiling cases)")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="tokens per GPU (default 24576; cfg5 default 4096; smaller for profiling cases)")
     ap.add_argument("--experts", type=int, default=0, help="override the number of experts (profiling cases)")
     return ap.parse_args()
 
@@ -141,24 +143,29 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------- workload
 
 def build_workload(args, rank, world, device):
-    import torch
-
-    from cutlass_op.bf16_grouped_mm.workloads import MoEShape, make_weights_device, offs_from_counts, zipf_routing
-
+    """(name, description, E, forced-empty experts, tokens, top-k, H, I, zipf s, forward only)."""
     wl = args.workload if args.workload != "auto" else ("cfg3" if world == 1 else "cfg4")
-    tokens, topk, H, I = args.tokens, 4, 2880, 2880
-    if wl == "cfg3":
+    if wl == "cfg5":
+        tokens = args.tokens or 4096
+        E_total = args.experts or 256
+        desc = (f"cfg5: fine-grained E={E_total} H=7168 I=2048, {tokens} tokens top-8 Zipf(1.3) with forced "
+                f"groups of 0, 1, 7 and 129 rows, fwd+bwd")
+        return wl, desc, E_total, 0, tokens, 8, 7168, 2048, 1.3, False
+    tokens, topk, H, I = args.tokens or 24576, 4, 2880, 2880
+    if wl in ("cfg2", "cfg3"):
         E_total = args.experts or 32
-        zero = 2
-        desc = (f"cfg3: GPT-OSS-20B experts E={E_total} H=I=2880, {tokens} tokens top-4 Zipf(1.1), "
-                f"2 experts with 0 tokens")
-    else:
-        E_total = args.experts or 128
-        zero = 0
-        desc = (f"cfg4: GPT-OSS-120B experts E=128 H=I=2880, 24576 tokens/rank top-4 {args.routing} routing, "
-                f"expert parallel E/{world} per GPU, dispatch/combine by "
-                + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all"))
-    return wl, desc, E_total, zero, tokens, topk, H, I
+        zero = 2 if wl == "cfg3" else 0
+        if wl == "cfg3":
+            desc = (f"cfg3: GPT-OSS-20B experts E={E_total} H=I=2880, {tokens} tokens top-4 Zipf(1.1), "
+                    f"2 experts with 0 tokens")
+        else:
+            desc = f"cfg2: forward-only grouped_mm_swiglu, E={E_total} H=I=2880, {tokens} tokens top-4 Zipf(1.1)"
+        return wl, desc, E_total, zero, tokens, topk, H, I, 1.1, wl == "cfg2"
+    E_total = args.experts or 128
+    desc = (f"cfg4: GPT-OSS-120B experts E=128 H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
+            f"expert parallel E/{world} per GPU, dispatch/combine by "
+            + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all"))
+    return wl, desc, E_total, 0, tokens, topk, H, I, 1.1, False
 
 
 # ------------------------------------------------------------------------------------- runs
@@ -270,12 +277,17 @@ def main():
     from cutlass_op.bf16_grouped_mm.optimer import OpTimer
     from cutlass_op.bf16_grouped_mm.workloads import MoEShape, make_weights_device, offs_from_counts, zipf_routing
 
-    wl, desc, E_total, zero, tokens, topk, H, I = build_workload(args, rank, world, device)
+    wl, desc, E_total, zero, tokens, topk, H, I, zipf_s, fwd_only = build_workload(args, rank, world, device)
     peaks, peak_src = load_peaks()
 
     if world == 1:
         E = E_total
-        counts = zipf_routing(tokens, E, topk, 1.1, seed=0, zero_experts=zero)
+        if wl == "cfg5":
+            from cutlass_op.bf16_grouped_mm.workloads import config5_counts
+
+            counts = config5_counts(tokens, E, topk, seed=0)
+        else:
+            counts = zipf_routing(tokens, E, topk, zipf_s, seed=0, zero_experts=zero)
         M = int(counts.sum())
         offs = offs_from_counts(counts).to(device)
         gx = torch.Generator(device=device).manual_seed(1)
@@ -287,6 +299,10 @@ def main():
         def step():
             for p in params:
                 p.grad = None
+            if fwd_only:
+                with torch.no_grad():
+                    mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
+                return
             s, aux = mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
             out = mgf.grouped_mm_downproj(s, w_down, offs, b_down, aux, ALPHA, LIMIT)
             out.sum().backward()
@@ -325,7 +341,7 @@ def main():
     ops = timer.summary()
     if world > 1:
         local_rows = int(ffn.last_local_rows)
-    flops_local = 18.0 * local_rows * H * I
+    flops_local = (4.0 if fwd_only else 18.0) * local_rows * H * I
     t = torch.tensor([ms, flops_local], dtype=torch.float64, device=device)
     if world > 1:
         tmax = t.clone()
@@ -362,8 +378,9 @@ def main():
         "config": {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
                    "routed_rows_gpu0": local_rows, "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (x 566 MB + weights >= 1.6 GB per GPU), no flush",
-                   "step": "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
-                           "(the metric is the MoE FFN fwd+bwd)"},
+                   "step": ("grouped_mm_swiglu forward only (config 2)" if fwd_only else
+                            "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
+                            "(the metric is the MoE FFN fwd+bwd)")},
         "tflops_per_gpu": per_gpu,
         "pct_of_peak": 100.0 * per_gpu / peaks["bf16_tflops_sustained"],
         "peak_tflops": peaks["bf16_tflops_sustained"], "peak_source": f"{peak_src} bf16_tflops_sustained",
@@ -375,11 +392,12 @@ def main():
     # torch._grouped_mm + eager bias/SwiGLU on the same inputs (single GPU only)
     if world == 1 and not args.no_compare:
         line["torch_grouped_mm"] = compare_torch(step_inputs=(x, w_up, b_up, w_down, b_down, offs, counts),
-                                                 steps=args.steps, warmup=args.warmup, flops=flops_local)
+                                                 steps=args.steps, warmup=args.warmup, flops=flops_local,
+                                                 fwd_only=fwd_only)
 
     # end-to-end through the public API with host buffers
     if world == 1 and not args.no_e2e:
-        line["e2e"] = e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops_local)
+        line["e2e"] = e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops_local, fwd_only)
 
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tf, rows, t = cpu_sample_tflops(H, I, target_s=12.0, max_rows=65536)
@@ -393,7 +411,7 @@ def main():
         dist.destroy_process_group()
 
 
-def compare_torch(step_inputs, steps, warmup, flops):
+def compare_torch(step_inputs, steps, warmup, flops, fwd_only=False):
     import torch
 
     x, w_up, b_up, w_down, b_down, offs, counts = step_inputs
@@ -407,6 +425,13 @@ def compare_torch(step_inputs, steps, warmup, flops):
         def step():
             for p in params:
                 p.grad = None
+            if fwd_only:
+                with torch.no_grad():
+                    h = torch._grouped_mm(xs, wu, offs=offs) + bu[row_e]
+                    g = h[:, 0::2].clamp(max=LIMIT)
+                    u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
+                    g * torch.sigmoid(ALPHA * g) * (u + 1.0)
+                return
             h = torch._grouped_mm(xs, wu, offs=offs) + bu[row_e]
             g = h[:, 0::2].clamp(max=LIMIT)
             u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
@@ -423,7 +448,7 @@ def compare_torch(step_inputs, steps, warmup, flops):
         return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 
 
-def e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops):
+def e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops, fwd_only=False):
     """Public-API step with the step's inputs copied from pinned host memory and the loss read back."""
     import torch
 
@@ -439,6 +464,11 @@ def e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops):
             p.grad = None
         x_dev.copy_(x_host, non_blocking=True)
         offs_dev.copy_(offs_host, non_blocking=True)
+        if fwd_only:
+            with torch.no_grad():
+                s, _ = mgf.grouped_mm_swiglu(x_dev, w_up, offs_dev, b_up, ALPHA, LIMIT)
+                loss_host.copy_(s.float().sum(), non_blocking=True)
+            return
         xl = x_dev.detach().requires_grad_(True)
         s, aux = mgf.grouped_mm_swiglu(xl, w_up, offs_dev, b_up, ALPHA, LIMIT)
         out = mgf.grouped_mm_downproj(s, w_down, offs_dev, b_down, aux, ALPHA, LIMIT)

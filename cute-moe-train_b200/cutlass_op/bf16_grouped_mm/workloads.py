@@ -58,6 +58,40 @@ def zipf_routing(tokens: int, E: int, topk: int, s: float, seed: int, zero_exper
     return counts.to(device)
 
 
+def force_group_sizes(counts: torch.Tensor, sizes=(0, 1, 7, 129), seed: int = 0) -> torch.Tensor:
+    """Config 5's forced ragged groups: give len(sizes) seeded experts (never the largest) exactly
+    those token counts, keeping the total: the surplus goes to the largest expert, a deficit is taken
+    from the largest experts in turn (never below zero)."""
+    counts = counts.clone()
+    g = torch.Generator(device="cpu").manual_seed(seed + 17)
+    big = int(torch.argmax(counts))
+    cand = [int(e) for e in torch.randperm(counts.numel(), generator=g) if int(e) != big][: len(sizes)]
+    delta = 0
+    for e, sz in zip(cand, sizes):
+        delta += int(counts[e]) - sz
+        counts[e] = sz
+    if delta >= 0:
+        counts[big] += delta
+    else:
+        need = -delta
+        for e in torch.argsort(counts, descending=True).tolist():
+            if e in cand:
+                continue
+            take = min(need, int(counts[e]))
+            counts[e] -= take
+            need -= take
+            if need == 0:
+                break
+        if need:
+            raise ValueError("force_group_sizes: not enough tokens to force the requested group sizes")
+    return counts
+
+
+def config5_counts(tokens: int, E: int = 256, topk: int = 8, seed: int = 0) -> torch.Tensor:
+    """Config 5 routing: top-8 of Zipf(1.3) over 256 experts, then forced groups of 0, 1, 7 and 129."""
+    return force_group_sizes(zipf_routing(tokens, E, topk, 1.3, seed=seed), seed=seed)
+
+
 def offs_from_counts(counts: torch.Tensor) -> torch.Tensor:
     return torch.cumsum(counts.to(torch.int64), 0).to(torch.int32)
 

@@ -136,3 +136,16 @@ def test_fused_only_contract():
     s, aux = m.grouped_mm_swiglu(xl, w_up.cuda(), offs.cuda(), b_up.cuda())
     with pytest.raises(RuntimeError, match="fused-only"):
         s.float().sum().backward()
+
+
+def test_config5_style_fine_grained_groups():
+    """Config 5's structure at small widths: 256 experts, top-8, Zipf(1.3) plus forced groups of
+    0, 1, 7 and 129 rows -- most groups tiny or empty."""
+    from cutlass_op.bf16_grouped_mm.workloads import config5_counts, small_case
+
+    counts = config5_counts(96, 256, 8, seed=3)
+    assert sorted(counts.tolist()).count(0) >= 1 and 129 in counts.tolist() and 7 in counts.tolist()
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(256, 64, 32, counts.tolist(), seed=5)
+    got = _run_chain(x, w_up, b_up, w_down, b_down, offs, gout)
+    ref = O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, gout)
+    _compare_chain(got, ref, offs)

@@ -101,3 +101,13 @@ def test_zipf_routing_properties():
     offs = offs_from_counts(c)
     assert offs.dtype == torch.int32 and int(offs[-1]) == 24576 * 4
     assert torch.equal(zipf_routing(24576, 32, 4, 1.1, seed=0, zero_experts=2), c)
+
+
+def test_config5_forced_group_sizes():
+    from cutlass_op.bf16_grouped_mm.workloads import config5_counts
+
+    for tokens in (64, 96, 4096):
+        c = config5_counts(tokens, 256, 8, seed=1)
+        assert int(c.sum()) == tokens * 8 and int(c.min()) >= 0
+        for sz in (0, 1, 7, 129):
+            assert sz in c.tolist()
