@@ -58,9 +58,12 @@ struct TileCfg {
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int BAR_BYTES = 384;
   static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
-  static constexpr int BUDGET = 227 * 1024 - 1024 - BAR_BYTES - SCHED_BYTES;
+  static constexpr int OUT_CHUNK_BYTES = BM * 32 * 2;                // one 128 x 32 bf16 output chunk
+  static constexpr int OUT_BYTES = kEpiGroups * OUT_CHUNK_BYTES;     // TMA-store staging (ragged-K)
+  static constexpr int OUT_OFFSET = (BAR_BYTES + SCHED_BYTES + 1023) / 1024 * 1024;  // after the stages
+  static constexpr int BUDGET = 227 * 1024 - 1024 - OUT_OFFSET - OUT_BYTES;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + SCHED_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + OUT_OFFSET + OUT_BYTES;
   static_assert(STAGES >= 3, "pipeline depth");
   static_assert((3 * STAGES + 5 + 2 * kRing) * 8 + 16 <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -268,7 +271,7 @@ __device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, i
 template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const Params p) {
+                        const __grid_constant__ CUtensorMap tmD, const Params p) {
   using Cfg = TileCfg<BN, CG, B_MN>;
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
   constexpr int STAGES = Cfg::STAGES;
@@ -291,6 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* ring_ids = reinterpret_cast<volatile int*>(tmem_holder + 2);
   int* sched = reinterpret_cast<int*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
+  uint8_t* out_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::OUT_OFFSET;  // 1024-aligned
   SchedSmem ss{sched, sched + (kMaxGroups + 1), sched + 2 * (kMaxGroups + 1)};
 
   const int warp = threadIdx.x >> 5;
@@ -682,14 +686,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
         ptx::tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-        // ragged-K weight gradient: rows are output features m0 + r
+        // ragged-K weight gradient: rows are output features m0 + r.  dW [E, m, n] is dense, so each
+        // warp stages its 32 rows x 32 columns in its own shared-memory slice and lane 0 stores it
+        // with one TMA tile store (clipped at m and n by the tensor map); no cross-warp sync.
         const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
         const int frow = m0 + r;
         int ones_r = -1;
         if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
-        const bool row_out = frow < p.m;
         const bool row_bias = (r == ones_r);
-        const bool warp_active = (m0 + q * 32 < p.m) || (ones_r >= q * 32 && ones_r < q * 32 + 32);
+        const bool warp_rows = m0 + q * 32 < p.m;  // this warp holds rows of dW
+        const bool warp_active = warp_rows || (ones_r >= q * 32 && ones_r < q * 32 + 32);
+        uint8_t* slice = out_stage + (warp - 2) * (32 * 64);
+        const uint32_t slice_u32 = ptx::smem_u32(slice);
         if (warp_active) {
 #pragma unroll 1
           for (int c = c_begin; c < c_begin + kChunks; ++c) {
@@ -706,10 +714,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int h = 0; h < 16; ++h) packed[h] = 0u;
             }
-            uint4* dp = nullptr;
-            if (row_out) dp = reinterpret_cast<uint4*>(p.d + (int64_t)ti.e * p.ldd_batch + (int64_t)frow * p.ldd + col0);
-            else if (row_bias) dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
-            if (dp != nullptr) {
+            if (warp_rows) {
+              if (lane == 0) ptx::bulk_wait_read_all();  // the slice's previous store has read it
+              __syncwarp();
+              // 64-byte swizzle (matches the tensor map): 16-byte unit g of row `lane` at g ^ ((lane >> 1) & 3)
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                *reinterpret_cast<uint4*>(slice + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                ptx::tma_store_3d(&tmD, slice_u32, col0, m0 + q * 32, ti.e);
+                ptx::bulk_commit();
+              }
+            }
+            if (row_bias) {
+              uint4* dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
 #pragma unroll
               for (int g = 0; g < 4; ++g)
                 if (col0 + 8 * g < p.n)
@@ -727,6 +748,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if constexpr (RAGGED_K) {
+    if (warp >= 2 && lane == 0) ptx::bulk_wait_all();  // this warp's tile stores are complete
+  }
   ptx::tc_fence_before();
   __syncthreads();
   // A pair leaves together: the peer may still signal this CTA's barriers until both are done.
@@ -760,7 +784,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                        const uint32_t* box) {
+                        const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = get_encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t d[3];
@@ -773,7 +797,7 @@ static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64
   }
   for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     snprintf(g_last_error, sizeof(g_last_error), "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
@@ -813,7 +837,8 @@ static bool debug_sync() {
 }
 
 template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
-static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid_in, cudaStream_t st) {
+static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD, const Params& p,
+                       int grid_in, cudaStream_t st) {
   int grid = grid_in;
   auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG>;
   constexpr int smem = TileCfg<BN, CG, B_MN>::SMEM_BYTES;
@@ -858,11 +883,11 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Param
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess && debug_sync()) fprintf(stderr, "[mgf] cleared pre-existing error: %s\n", cudaGetErrorString(e));
   if constexpr (CG == 1) {
-    kern<<<grid, kThreads, smem, st>>>(tA, tB, p);
+    kern<<<grid, kThreads, smem, st>>>(tA, tB, tD, p);
     e = cudaGetLastError();
   } else {
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    e = cudaLaunchKernelEx(&cfg, kern, tA, tB, p);
+    e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tD, p);
   }
   if (e != cudaSuccess) {
     record_error("kernel launch", e);
@@ -881,20 +906,20 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const Param
 }
 
 template <int BN, int CG>
-static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtensorMap& tB, const Params& p, int grid,
-                        cudaStream_t st) {
+static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD,
+                        const Params& p, int grid, cudaStream_t st) {
   switch (epi) {
     case MGF_EPI_BIAS:
-      return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true, CG>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_BIAS, false, false, CG>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true, CG>(tA, tB, tD, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_BIAS, false, false, CG>(tA, tB, tD, p, grid, st);
     case MGF_EPI_SWIGLU:
-      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU, false, true, CG>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_SWIGLU, false, false, CG>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU, false, true, CG>(tA, tB, tD, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU, false, false, CG>(tA, tB, tD, p, grid, st);
     case MGF_EPI_SWIGLU_BWD:
-      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true, CG>(tA, tB, p, grid, st)
-                  : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false, CG>(tA, tB, p, grid, st);
+      return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true, CG>(tA, tB, tD, p, grid, st)
+                  : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false, CG>(tA, tB, tD, p, grid, st);
     case MGF_EPI_WGRAD:
-      return launch_inst<BN, MGF_EPI_WGRAD, true, true, CG>(tA, tB, p, grid, st);
+      return launch_inst<BN, MGF_EPI_WGRAD, true, true, CG>(tA, tB, tD, p, grid, st);
     default:
       return MGF_ERR_INVALID_ARGUMENT;
   }
@@ -1033,7 +1058,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   if (!stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
   if (!no_rows && (!stride_ok(g.lda) || !stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
 
-  CUtensorMap tA, tB;
+  CUtensorMap tA, tB, tD;
   int bn, n_tiles, cg = 1;
   int64_t tiles_upper;
   if (!ragged_k) {
@@ -1061,6 +1086,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
     const uint32_t bA[2] = {64, 128};
     if (!encode_bf16(&tA, g.a, 2, dA, sA, bA)) return MGF_ERR_CUDA;
+    tD = tA;  // unused by the ragged-M epilogues
     const uint64_t sB[2] = {static_cast<uint64_t>(g.ldb) * 2, static_cast<uint64_t>(g.ldb_batch) * 2};
     if (g.b_mn_major) {
       const uint64_t dB[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.num_groups)};
@@ -1103,6 +1129,11 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
       if (!encode_bf16(&tA, g.d, 2, dz, sz, box) || !encode_bf16(&tB, g.d, 2, dz, sz, box)) return MGF_ERR_CUDA;
     }
     tiles_upper = static_cast<int64_t>(p.m_tiles) * n_tiles * g.num_groups;
+    // dW [E, m, n] for the epilogue's TMA tile stores: 32 x 32 boxes, 64-byte swizzle
+    const uint64_t dD[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.num_groups)};
+    const uint64_t sD[2] = {static_cast<uint64_t>(g.ldd) * 2, static_cast<uint64_t>(g.ldd_batch) * 2};
+    const uint32_t bD[3] = {32, 32, 1};
+    if (!encode_bf16(&tD, g.d, 3, dD, sD, bD, CU_TENSOR_MAP_SWIZZLE_64B)) return MGF_ERR_CUDA;
   }
 
   int sms = di.sms - (g.sm_carveout > 0 ? g.sm_carveout : 0);
@@ -1125,15 +1156,15 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   }
   if (cg == 2) {
     switch (bn) {
-      case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
-      case 192: return dispatch_epi<192, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
-      default: return dispatch_epi<128, 2>(g.epilogue, b_mn, tA, tB, p, grid, st);
+      case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+      case 192: return dispatch_epi<192, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+      default: return dispatch_epi<128, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
     }
   }
   switch (bn) {
-    case 256: return dispatch_epi<256, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
-    case 192: return dispatch_epi<192, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
-    default: return dispatch_epi<128, 1>(g.epilogue, b_mn, tA, tB, p, grid, st);
+    case 256: return dispatch_epi<256, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+    case 192: return dispatch_epi<192, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+    default: return dispatch_epi<128, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
   }
 }
 
