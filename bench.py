@@ -191,7 +191,8 @@ def time_steps(step_fn, steps, warmup, barrier=None, sync=None):
 
 
 def cpu_sample_tflops(H, I, target_s, max_rows=16384):
-    """Time the oracle (CPU restatement of the reference's chain) fwd+bwd on S rows of the shape."""
+    """Time the oracle (CPU restatement of the reference's chain) fwd+bwd on S rows of the shape,
+    repeated until at least target_s seconds of CPU work were timed; returns (TFLOP/s, S, seconds)."""
     import torch
 
     from cutlass_op.bf16_grouped_mm.workloads import small_case
@@ -199,20 +200,25 @@ def cpu_sample_tflops(H, I, target_s, max_rows=16384):
 
     torch.set_num_threads(os.cpu_count() or 1)
 
-    def run(rows):
-        counts = [rows // 2, rows - rows // 2]
-        x, wu, bu, wd, bd, offs, g = small_case(2, H, I, counts, seed=123)
+    def case(rows):
+        return small_case(2, H, I, [rows // 2, rows - rows // 2], seed=123)
+
+    def run(c):
         t0 = time.perf_counter()
-        O.kernel_chain(x, wu, bu, wd, bd, offs, g)
+        O.kernel_chain(*c)
         return time.perf_counter() - t0
 
-    rows = 256
-    t = run(rows)
-    rows = int(max(256, min(max_rows, rows * target_s / max(t, 1e-3))))
+    rows = 1024
+    t = run(case(rows))
+    rows = int(max(256, min(max_rows, rows * (target_s / 4) / max(t, 1e-3))))
     rows -= rows % 8
-    t = run(rows)
-    flops = 18.0 * rows * H * I
-    return flops / t / 1e12, rows, t
+    c = case(rows)
+    total, reps = 0.0, 0
+    while total < target_s and reps < 50:
+        total += run(c)
+        reps += 1
+    flops = 18.0 * rows * H * I * reps
+    return flops / total / 1e12, rows, total
 
 
 def reference_arm(args, rank, world):
@@ -404,7 +410,7 @@ def main():
         import torch as _t
         line["cpu_baseline"] = {"value": tf, "unit": UNIT, "cores": _t.get_num_threads(), "kind": "port",
                                 "sample": f"oracle fwd+bwd on {rows} routed rows over 2 experts of the H=I=2880 "
-                                          f"shape ({t:.1f} s), fp32 torch on the host"}
+                                          f"shape, repeated for {t:.1f} s of CPU work, fp32 torch on the host"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
