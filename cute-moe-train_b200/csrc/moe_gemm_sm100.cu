@@ -56,7 +56,7 @@ struct TileCfg {
   static constexpr int B_BYTES = B_MN ? B_CHUNKS * 8192 : BNC * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int BAR_BYTES = 384;
+  static constexpr int BAR_BYTES = 512;
   static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
   static constexpr int OUT_CHUNK_BYTES = BM * 32 * 2;                // one 128 x 32 bf16 output chunk
   static constexpr int OUT_BYTES = kEpiGroups * OUT_CHUNK_BYTES;     // TMA-store staging (ragged-K)
@@ -65,7 +65,7 @@ struct TileCfg {
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + OUT_OFFSET + OUT_BYTES;
   static_assert(STAGES >= 3, "pipeline depth");
-  static_assert((3 * STAGES + 5 + 2 * kRing) * 8 + 16 <= BAR_BYTES, "barrier area");
+  static_assert((3 * STAGES + 5 + 4 * kRing) * 8 + 8 + 8 * kRing <= BAR_BYTES, "barrier area");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -242,14 +242,11 @@ __device__ __forceinline__ uint32_t swiglu_bwd_word(float gs, uint32_t aux_word,
 template <int A_CHUNKS, int B_CHUNKS>
 __device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, int ones_local, int lane) {
   constexpr int kChunks = A_CHUNKS + B_CHUNKS;
-  const int nrows = BK - valid_k;
-  const int n16 = nrows * 8 * kChunks;
-  for (int i = lane; i < n16; i += 32) {
-    const int chunk = i / (nrows * 8);
-    const int rem = i - chunk * nrows * 8;
-    const int row = valid_k + rem / 8;
-    const int col16 = rem & 7;
-    *reinterpret_cast<uint4*>(sA + chunk * 8192 + row * 128 + col16 * 16) = make_uint4(0, 0, 0, 0);
+  // 16-byte unit u of a chunk is K row u / 8 (8 units per 128-byte row): clear units 8*valid_k..511
+  // of every chunk, the same unit of all chunks per iteration (the chunks are 8 KB apart).
+  for (int u = valid_k * 8 + lane; u < BK * 8; u += 32) {
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) *reinterpret_cast<uint4*>(sA + c * 8192 + u * 16) = make_uint4(0, 0, 0, 0);
   }
   if (ones_local >= 0) {
     // The A feature row past m reads as zero (TMA out-of-bounds fill); 1.0 in its valid K rows makes
@@ -290,9 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* ring_full = bars + 2 * STAGES + 5;
   uint64_t* ring_empty = bars + 2 * STAGES + 5 + kRing;
   uint64_t* patch_done = bars + 2 * STAGES + 5 + 2 * kRing;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5 + 2 * kRing);
+  uint64_t* mbox_full = bars + 3 * STAGES + 5 + 2 * kRing;   // odd CTA: tile id posted by the leader
+  uint64_t* mbox_empty = bars + 3 * STAGES + 5 + 3 * kRing;  // leader: the odd CTA took the id
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5 + 4 * kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* ring_ids = reinterpret_cast<volatile int*>(tmem_holder + 2);
+  volatile int* mbox_ids = ring_ids + kRing;
   int* sched = reinterpret_cast<int*>(smem + STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES);
   uint8_t* out_stage = smem + STAGES * Cfg::STAGE_BYTES + Cfg::OUT_OFFSET;  // 1024-aligned
   SchedSmem ss{sched, sched + (kMaxGroups + 1), sched + 2 * (kMaxGroups + 1)};
@@ -318,6 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < kRing; ++j) {
       ptx::mbar_init(ptx::smem_u32(&ring_full[j]), 1);
       ptx::mbar_init(ptx::smem_u32(&ring_empty[j]), 1 + kNumEpiWarps);
+      ptx::mbar_init(ptx::smem_u32(&mbox_full[j]), 1);
+      ptx::mbar_init(ptx::smem_u32(&mbox_empty[j]), 1);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -376,11 +378,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // The producer picks the tile sequence (static striding, or an atomic counter when the
       // launch has one) and hands every tile id to the MMA and epilogue warps through the ring.
+      // A pair with a counter: the even CTA claims each tile and posts its id into the odd CTA's
+      // mailbox (a remote store, then a release arrive on the odd CTA's barrier).
+      const bool forwarded = (CG == 2) && (p.tile_counter != nullptr);
       int t = unit;
       uint32_t rslot = 0, rphase = 0;
+      uint32_t mslot = 0, mphase = 0;
       while (ok && !p.stall_test) {
         if (!wait_bounded(ptx::smem_u32(&ring_empty[rslot]), rphase ^ 1, abort_flag)) { ok = false; break; }
-        const int tt = t < total_tiles ? t : -1;
+        if (forwarded) {
+          if (leader) {
+            if (!wait_bounded<true>(ptx::smem_u32(&mbox_empty[mslot]), mphase ^ 1, abort_flag)) { ok = false; break; }
+            ptx::st_cluster_u32(ptx::mapa_shared(ptx::smem_u32(const_cast<int*>(&mbox_ids[mslot])), 1),
+                                static_cast<uint32_t>(t < total_tiles ? t : -1));
+            ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&mbox_full[mslot]), 1));
+          } else {
+            if (!wait_bounded<true>(ptx::smem_u32(&mbox_full[mslot]), mphase, abort_flag)) { ok = false; break; }
+            t = mbox_ids[mslot];
+            ptx::mbar_arrive_cluster(leader_addr(&mbox_empty[mslot]));
+          }
+          if (++mslot == kRing) { mslot = 0; mphase ^= 1; }
+        }
+        const int tt = (t >= 0 && t < total_tiles) ? t : -1;
         ring_ids[rslot] = tt;
         ptx::mbar_arrive(ptx::smem_u32(&ring_full[rslot]));
         if (++rslot == kRing) { rslot = 0; rphase ^= 1; }
@@ -435,7 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued_parity[stage] = phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        t = (p.tile_counter != nullptr) ? num_units + atomicAdd(p.tile_counter, 1) : t + num_units;
+        if (p.tile_counter == nullptr) t += num_units;
+        else if (leader) t = num_units + atomicAdd(p.tile_counter, 1);  // the odd CTA reads its mailbox
       }
       if (!ok && CG == 1) {
         // Stopped early: let the copies already in flight land before the CTA exits.  (A pair waits
@@ -690,7 +710,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp stages its 32 rows x 32 columns in its own shared-memory slice and lane 0 stores it
         // with one TMA tile store (clipped at m and n by the tensor map); no cross-warp sync.
         const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
-        const int frow = m0 + r;
         int ones_r = -1;
         if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
         const bool row_bias = (r == ones_r);
@@ -1146,7 +1165,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   const bool b_mn = ragged_k ? true : (g.b_mn_major != 0);
   // The dynamic tile counter serves single CTAs only: both CTAs of a pair must walk the same tile
   // sequence, which static striding gives them.
-  p.tile_counter = (g.epilogue == MGF_EPI_WGRAD && cg == 1) ? g.workspace : nullptr;
+  p.tile_counter = (g.epilogue == MGF_EPI_WGRAD) ? g.workspace : nullptr;
   // Test hook for the bounded waits: with MGF_TEST_STALL_PRODUCER=1 the kernel does no work and
   // every consumer wait gives up after its limit, setting MGF_DEV_WAIT_TIMEOUT.  Nothing is in flight
   // when they give up, so the context stays usable; tests use it to exercise that path on a GPU.

@@ -171,6 +171,11 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+// 32-bit store into shared memory of a CTA of this cluster (address from mapa_shared).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
