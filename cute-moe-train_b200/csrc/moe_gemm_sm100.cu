@@ -89,6 +89,8 @@ struct Params {
   int64_t ld_aux;
   float alpha, limit;
   int store_aux;
+  int aux_v8;         // aux base 32-byte aligned and row pitch a multiple of 32 bytes
+  int d_v8, d2_v8;    // the same for the ragged-M outputs d and d2
   int stall_test;     // test hook: the producer hands out no tiles, so every consumer wait runs out
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
 };
@@ -130,6 +132,49 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
         atomicOr(&g_status, MGF_DEV_WAIT_TIMEOUT);
         return false;
       }
+    }
+  }
+}
+
+
+#ifndef MGF_AUX_NOALLOC
+#define MGF_AUX_NOALLOC 1
+#endif
+// One chunk of aux words (32 packed (gate, up) pairs = 128 bytes of one row) as four 32-byte loads;
+// words past n read as zero.  Each sector is requested once, so nothing relies on L1 reuse.
+// v8 = false (aux rows only 16-byte aligned): eight 16-byte loads.
+__device__ __forceinline__ void load_aux_chunk(const __nv_bfloat16* row, int col0, int n, bool valid, bool v8,
+                                               uint4 (&aw)[8]) {
+  const uint4* ap = reinterpret_cast<const uint4*>(row + 2 * col0);
+  if (!v8) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g) aw[g] = (valid && col0 + 4 * g < n) ? __ldg(ap + g) : make_uint4(0, 0, 0, 0);
+    return;
+  }
+#pragma unroll
+  for (int g = 0; g < 8; g += 2) {
+    if (valid && col0 + 4 * g < n) {
+      if (MGF_AUX_NOALLOC) ptx::ld_nc_v8_noalloc(ap + g, aw[g], aw[g + 1]);
+      else ptx::ld_nc_v8(ap + g, aw[g], aw[g + 1]);
+    } else {
+      aw[g] = make_uint4(0, 0, 0, 0);
+      aw[g + 1] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Store the first `nvalid` of NU 16-byte units of one output row; pairs of units go out as one
+// 32-byte store when v8 (the row and its 32-byte pairs aligned).
+template <int NU>
+__device__ __forceinline__ void store_units(void* dst, const uint4 (&u)[NU], int nvalid, bool v8) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int g = 0; g < NU; g += 2) {
+    if (v8 && g + 1 < nvalid) {
+      ptx::st_v8(d + g, u[g], u[g + 1]);
+    } else {
+      if (g < nvalid) d[g] = u[g];
+      if (g + 1 < nvalid) d[g + 1] = u[g + 1];
     }
   }
 }
@@ -616,10 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // loads are issued before waiting for the mainloop.
         uint4 aw[8];
         if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
-          const int col0 = n0 + c_begin * 32;
-          const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * col0);
-#pragma unroll
-          for (int g = 0; g < 8; ++g) aw[g] = (valid && col0 + 4 * g < p.n) ? __ldg(ap + g) : make_uint4(0, 0, 0, 0);
+          load_aux_chunk(p.aux + (int64_t)grow * p.ld_aux, n0 + c_begin * 32, p.n, valid, p.aux_v8, aw);
         }
         if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
         ptx::tc_fence_after();
@@ -656,11 +698,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(f[2 * h], f[2 * h + 1]);
               if (EPI == MGF_EPI_BIAS || p.store_aux) {
-                uint4* dp = reinterpret_cast<uint4*>(p.d + (int64_t)grow * p.ldd + col0);
+                uint4 u[4];
 #pragma unroll
-                for (int g = 0; g < 4; ++g)
-                  if (col0 + 8 * g < p.n)
-                    dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+                for (int g = 0; g < 4; ++g) u[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+                store_units<4>(p.d + (int64_t)grow * p.ldd + col0, u, (p.n - col0) >> 3, p.d_v8);
               }
               if constexpr (EPI == MGF_EPI_SWIGLU) {
                 uint32_t so[8];
@@ -671,10 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                       swiglu_fwd(bf16_lo(packed[2 * h + 1]), bf16_hi(packed[2 * h + 1]), p.alpha, p.limit);
                   so[h] = pack_bf16x2(a0, a1);
                 }
-                uint4* sp = reinterpret_cast<uint4*>(p.d2 + (int64_t)grow * p.ldd2 + (col0 >> 1));
-#pragma unroll
-                for (int g = 0; g < 2; ++g)
-                  if (col0 + 16 * g < p.n) sp[g] = make_uint4(so[4 * g], so[4 * g + 1], so[4 * g + 2], so[4 * g + 3]);
+                const uint4 u[2] = {make_uint4(so[0], so[1], so[2], so[3]), make_uint4(so[4], so[5], so[6], so[7])};
+                store_units<2>(p.d2 + (int64_t)grow * p.ldd2 + (col0 >> 1), u, (p.n - col0) >> 4, p.d2_v8);
               }
             } else if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
               uint4 cur[8];
@@ -682,21 +721,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int g = 0; g < 8; ++g) cur[g] = aw[g];
               // prefetch the next chunk's aux words while this chunk is computed and stored
               const int ncol0 = col0 + 32;
-              if (c + 1 < c_begin + kChunks && ncol0 < p.n) {
-                const uint4* ap = reinterpret_cast<const uint4*>(p.aux + (int64_t)grow * p.ld_aux + 2 * ncol0);
-#pragma unroll
-                for (int g = 0; g < 8; ++g) aw[g] = (ncol0 + 4 * g < p.n) ? __ldg(ap + g) : make_uint4(0, 0, 0, 0);
-              }
+              if (c + 1 < c_begin + kChunks && ncol0 < p.n) load_aux_chunk(p.aux + (int64_t)grow * p.ld_aux, ncol0, p.n, true, p.aux_v8, aw);
+              // two 16-byte units (8 GEMM columns) at a time: computed, then stored
               uint4* gp = reinterpret_cast<uint4*>(p.d + (int64_t)grow * p.ldd + 2 * col0);
+              const int nvalid = (p.n - col0) >> 2;
 #pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                if (col0 + 4 * g < p.n) {
-                  uint4 o;
-                  o.x = swiglu_bwd_word(__uint_as_float(v[4 * g + 0]), cur[g].x, p.alpha, p.limit);
-                  o.y = swiglu_bwd_word(__uint_as_float(v[4 * g + 1]), cur[g].y, p.alpha, p.limit);
-                  o.z = swiglu_bwd_word(__uint_as_float(v[4 * g + 2]), cur[g].z, p.alpha, p.limit);
-                  o.w = swiglu_bwd_word(__uint_as_float(v[4 * g + 3]), cur[g].w, p.alpha, p.limit);
-                  gp[g] = o;
+              for (int g = 0; g < 8; g += 2) {
+                if (g < nvalid) {
+                  uint4 o[2];
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    o[h].x = swiglu_bwd_word(__uint_as_float(v[4 * (g + h) + 0]), cur[g + h].x, p.alpha, p.limit);
+                    o[h].y = swiglu_bwd_word(__uint_as_float(v[4 * (g + h) + 1]), cur[g + h].y, p.alpha, p.limit);
+                    o[h].z = swiglu_bwd_word(__uint_as_float(v[4 * (g + h) + 2]), cur[g + h].z, p.alpha, p.limit);
+                    o[h].w = swiglu_bwd_word(__uint_as_float(v[4 * (g + h) + 3]), cur[g + h].w, p.alpha, p.limit);
+                  }
+                  // n % 8 == 0 and g even: unit g valid implies unit g + 1 valid
+                  if (p.d_v8) ptx::st_v8(gp + g, o[0], o[1]);
+                  else {
+                    gp[g] = o[0];
+                    gp[g + 1] = o[1];
+                  }
                 }
               }
             }
@@ -1066,6 +1111,12 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.ldd2 = g.ldd2;
   p.aux = static_cast<const __nv_bfloat16*>(g.aux);
   p.ld_aux = g.ld_aux;
+  auto v8_ok = [](const void* ptr, int64_t ld) {
+    return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 31u) == 0 && (ld % 16) == 0;
+  };
+  p.aux_v8 = v8_ok(g.aux, g.ld_aux) ? 1 : 0;
+  p.d_v8 = v8_ok(g.d, g.ldd) ? 1 : 0;
+  p.d2_v8 = v8_ok(g.d2, g.ldd2) ? 1 : 0;
   p.alpha = g.swiglu_alpha;
   p.limit = g.swiglu_limit;
   p.store_aux = g.store_aux;
