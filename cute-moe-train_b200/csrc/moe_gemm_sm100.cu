@@ -78,6 +78,7 @@ struct Params {
   int m_tiles;        // ragged-K: tiles along m per group (incl. the extra bias-grad tile)
   int m_tiles_real;   // ragged-K: ceil(m / tile rows)
   int bias_grad;      // ragged-K: write D2
+  int a_chunked, b_chunked;  // ragged-K: tmA / tmB are 3D {64, rows, 64-column chunks}: one box per stage
   const int32_t* offs;
   const __nv_bfloat16* bias;
   int64_t bias_stride;
@@ -498,10 +499,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             const int kr = ti.k_start + kb * BK;
             const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
+            if (p.a_chunked) {
+              load3(sA, &tmA, 0, kr, m0 >> 6);
+            } else {
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c) load2(sA + c * 8192, &tmA, m0 + 64 * c, kr);
+              for (int c = 0; c < BM / 64; ++c) load2(sA + c * 8192, &tmA, m0 + 64 * c, kr);
+            }
+            if (p.b_chunked) {
+              load3(sB, &tmB, 0, kr, nb0 >> 6);
+            } else {
 #pragma unroll
-            for (int c = 0; c < Cfg::B_CHUNKS; ++c) load2(sB + c * 8192, &tmB, nb0 + 64 * c, kr);
+              for (int c = 0; c < Cfg::B_CHUNKS; ++c) load2(sB + c * 8192, &tmB, nb0 + 64 * c, kr);
+            }
           }
           outstanding[stage] = true;
           issued_parity[stage] = phase;
@@ -1194,12 +1203,32 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % tm) == 0) ? 1 : 0);
     const uint32_t box[2] = {64, 64};
     if (!no_rows) {
-      const uint64_t dA[2] = {static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.total_rows)};
-      const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
-      if (!encode_bf16(&tA, g.a, 2, dA, sA, box)) return MGF_ERR_CUDA;
-      const uint64_t dB[2] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.total_rows)};
-      const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb) * 2};
-      if (!encode_bf16(&tB, g.b, 2, dB, sB, box)) return MGF_ERR_CUDA;
+      // Where the feature count is a multiple of 64, a stage's 64-column chunks of an operand come
+      // in one 3D box: {64 features, 64 rows, chunks}, the chunk dimension 128 bytes apart (TMA
+      // clips it at the last chunk, so the m / n tails still read as zeros).  Otherwise one 2D box
+      // per chunk, clipped at m / n.
+      const uint32_t boxA3[3] = {64, 64, static_cast<uint32_t>(BM / 64)};
+      const uint32_t boxB3[3] = {64, 64, static_cast<uint32_t>((bn / cg + 63) / 64)};
+      p.a_chunked = (g.m % 64) == 0 ? 1 : 0;
+      p.b_chunked = (g.n % 64) == 0 ? 1 : 0;
+      if (p.a_chunked) {
+        const uint64_t dA[3] = {64, static_cast<uint64_t>(g.total_rows), static_cast<uint64_t>(g.m / 64)};
+        const uint64_t sA[2] = {static_cast<uint64_t>(g.lda) * 2, 128};
+        if (!encode_bf16(&tA, g.a, 3, dA, sA, boxA3)) return MGF_ERR_CUDA;
+      } else {
+        const uint64_t dA[2] = {static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.total_rows)};
+        const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
+        if (!encode_bf16(&tA, g.a, 2, dA, sA, box)) return MGF_ERR_CUDA;
+      }
+      if (p.b_chunked) {
+        const uint64_t dB[3] = {64, static_cast<uint64_t>(g.total_rows), static_cast<uint64_t>(g.n / 64)};
+        const uint64_t sB[2] = {static_cast<uint64_t>(g.ldb) * 2, 128};
+        if (!encode_bf16(&tB, g.b, 3, dB, sB, boxB3)) return MGF_ERR_CUDA;
+      } else {
+        const uint64_t dB[2] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.total_rows)};
+        const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb) * 2};
+        if (!encode_bf16(&tB, g.b, 2, dB, sB, box)) return MGF_ERR_CUDA;
+      }
     } else {
       // Never dereferenced (every group is empty): well-formed maps over the output buffer.
       const uint64_t dz[2] = {8, 1};
