@@ -39,7 +39,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # FLOPs of each operator per launch, in units of M*H*I (M routed rows on this GPU).
 OP_FLOP_UNITS = {
     "up_swiglu_fwd": 4, "down_fwd": 2, "down_wgrad_bias": 2, "down_dgrad_swiglu_bwd": 2,
-    "up_dgrad": 4, "up_wgrad_bias": 4,
+    "up_dgrad": 4, "up_wgrad_bias": 4, "up_recompute_aux": 4,
 }
 
 
@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
+    ap.add_argument("--recompute-aux", action="store_true",
+                    help="store_aux=False: the forward keeps no aux, the backward recomputes it "
+                         "(the extra GEMM's FLOPs are not counted in the metric)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tokens", type=int, default=0,
@@ -309,8 +312,11 @@ def main():
                 with torch.no_grad():
                     mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
                 return
-            s, aux = mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
-            out = mgf.grouped_mm_downproj(s, w_down, offs, b_down, aux, ALPHA, LIMIT)
+            if args.recompute_aux:
+                out = mgf.grouped_mm_ffn(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT, store_aux=False)
+            else:
+                s, aux = mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
+                out = mgf.grouped_mm_downproj(s, w_down, offs, b_down, aux, ALPHA, LIMIT)
             out.sum().backward()
         local_rows = M
     else:
@@ -386,7 +392,9 @@ def main():
                    "l2": "inputs larger than L2 (x 566 MB + weights >= 1.6 GB per GPU), no flush",
                    "step": ("grouped_mm_swiglu forward only (config 2)" if fwd_only else
                             "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
-                            "(the metric is the MoE FFN fwd+bwd)")},
+                            "(the metric is the MoE FFN fwd+bwd)"
+                            + ("; store_aux=False: aux recomputed in backward, 18*M*H*I FLOPs counted"
+                               if args.recompute_aux else ""))},
         "tflops_per_gpu": per_gpu,
         "pct_of_peak": 100.0 * per_gpu / peaks["bf16_tflops_sustained"],
         "peak_tflops": peaks["bf16_tflops_sustained"], "peak_source": f"{peak_src} bf16_tflops_sustained",

@@ -219,8 +219,10 @@ Tensor mm_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::optional<Ten
 }
 
 // ---------------------------------------------------------------- grouped_mm::mm_swiglu
-std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
-                                          const Tensor& bias, double alpha, double limit) {
+// store_aux = false is the reference binding's `_grouped_mm_swiglu_cuda(..., store_aux=False)`
+// (csrc/binding.cu:36-63): only swiglu_out is written and the returned aux is undefined.
+std::tuple<Tensor, Tensor> swiglu_launch(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                         const Tensor& bias, double alpha, double limit, bool store_aux) {
   TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm_swiglu: inputs must be CUDA tensors");
   const c10::cuda::CUDAGuard guard(mat_a.device());
   TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 3, "grouped_mm_swiglu requires mat_a 2D and mat_b 3D (ragged-M path)");
@@ -237,10 +239,27 @@ std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat
   check_bias(bias, mat_b.size(0), N);
   const int64_t M = mat_a.size(0);
   Tensor swiglu_out = at::empty_strided({M, N / 2}, {padded(N / 2), 1}, mat_a.options());
+  if (!store_aux) {
+    // the kernel writes no aux row; swiglu_out stands in as the (unwritten) aux destination
+    launch_ragged_m(MGF_EPI_SWIGLU, mat_a, mat_b, offs, &bias, swiglu_out, &swiglu_out, nullptr, alpha, limit,
+                    false, "grouped_mm_swiglu_noaux");
+    return {swiglu_out, Tensor()};
+  }
   Tensor aux_out = at::empty_strided({M, N}, {padded(N), 1}, mat_a.options());
   launch_ragged_m(MGF_EPI_SWIGLU, mat_a, mat_b, offs, &bias, aux_out, &swiglu_out, nullptr, alpha, limit, true,
                   "grouped_mm_swiglu");
   return {swiglu_out, aux_out};
+}
+
+std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                          const Tensor& bias, double alpha, double limit) {
+  return swiglu_launch(mat_a, mat_b, offs, bias, alpha, limit, true);
+}
+
+// ---------------------------------------------------------------- grouped_mm::mm_swiglu_noaux
+Tensor mm_swiglu_noaux_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
+                            double alpha, double limit) {
+  return std::get<0>(swiglu_launch(mat_a, mat_b, offs, bias, alpha, limit, false));
 }
 
 // ---------------------------------------------------------------- grouped_mm::mm_swiglu_bwd
@@ -391,6 +410,9 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def(
       "mm_downproj(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor aux_biased_acc,"
       " float swiglu_alpha, float swiglu_limit) -> Tensor");
+  m.def(
+      "mm_swiglu_noaux(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha,"
+      " float swiglu_limit) -> Tensor");
   m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
   m.def("gather_rows(Tensor src, Tensor idx, Tensor? scale) -> Tensor");
   m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
@@ -402,6 +424,7 @@ TORCH_LIBRARY(grouped_mm, m) {
 TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm", &mm_cuda);
   m.impl("mm_swiglu", &mm_swiglu_cuda);
+  m.impl("mm_swiglu_noaux", &mm_swiglu_noaux_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
   m.impl("gather_rows", &gather_rows_cuda);

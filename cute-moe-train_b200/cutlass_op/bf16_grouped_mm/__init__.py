@@ -81,6 +81,28 @@ def grouped_mm_downproj(
         )
 
 
+def grouped_mm_ffn(
+    x: torch.Tensor,
+    w_up: torch.Tensor,
+    w_down: torch.Tensor,
+    offs: torch.Tensor,
+    b_up: torch.Tensor,
+    b_down: torch.Tensor | None = None,
+    swiglu_alpha: float = 1.702,
+    swiglu_limit: float = 7.0,
+    store_aux: bool = True,
+) -> torch.Tensor:
+    """The whole MoE expert FFN: ``grouped_mm_downproj(grouped_mm_swiglu(x, w_up) ...)``.
+
+    ``store_aux=True`` keeps ``aux_biased_acc`` [total_M, 2*I] from the forward for the backward,
+    like the two wrappers chained.  ``store_aux=False`` is the reference binding's recompute mode:
+    the forward does not write aux and the backward recomputes it with one more grouped GEMM
+    (same results, bit for bit; 4*M*H*I more FLOPs per step, rows x 2I x 2 bytes less memory).
+    """
+    return _custom_op.GroupedFFN.apply(x, w_up, b_up, w_down, b_down, offs, swiglu_alpha, swiglu_limit, store_aux)
+
+
+# The reference's exports; grouped_mm_ffn is an addition, imported by name.
 __all__ = [
     "grouped_mm",
     "grouped_mm_downproj",

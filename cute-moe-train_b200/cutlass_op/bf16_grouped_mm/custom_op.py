@@ -15,6 +15,8 @@ shape inference and autograd with the same contract as Butterfingrz/CuTe-MoE-Tra
 * ``grouped_mm::mm_swiglu_bwd`` (custom_op.py:534-571): opaque down-proj dgrad + SwiGLU backward.
 * ``grouped_mm::mm_downproj`` (custom_op.py:579-693): down-projection whose backward emits
   ``grad_aux`` for ``mm_swiglu`` instead of a gradient for ``swiglu_out``.
+* ``grouped_mm::mm_swiglu_noaux`` and :class:`GroupedFFN`: the ``store_aux=False`` recompute path
+  of the reference's binding (csrc/binding.cu:36-63) as a whole-FFN autograd function.
 """
 
 from __future__ import annotations
@@ -329,6 +331,96 @@ def _downproj_backward(ctx, grad_out):
 torch.library.register_autograd(
     "grouped_mm::mm_downproj", _downproj_backward, setup_context=_downproj_setup_context
 )
+
+# ============================================================================ grouped_mm::mm_swiglu_noaux
+
+
+@torch.library.register_fake("grouped_mm::mm_swiglu_noaux")
+def _swiglu_noaux_fake(mat_a, mat_b, offs, bias, swiglu_alpha, swiglu_limit):
+    half = mat_b.size(-1) // 2
+    return torch.empty_strided(
+        (mat_a.size(0), half), (_padded(half, torch.bfloat16), 1), dtype=torch.bfloat16, device=mat_a.device
+    )
+
+
+# ============================================================================ whole FFN, aux optional
+
+
+class GroupedFFN(torch.autograd.Function):
+    """Up-projection + bias + SwiGLU -> down-projection + bias, with autograd.
+
+    ``store_aux=True`` is exactly ``grouped_mm_swiglu`` followed by ``grouped_mm_downproj``.
+    ``store_aux=False`` is the recompute path of the reference's binding
+    (``_grouped_mm_swiglu_cuda(..., store_aux=False)``, csrc/binding.cu:36-63): the forward writes
+    no ``aux_biased_acc`` (saving rows x 2I bf16 of memory between forward and backward) and the
+    backward rebuilds it with one ragged-M GEMM + bias before the fused SwiGLU backward.  The
+    rebuilt aux equals the stored one bit for bit: the same tiles accumulate in the same order and
+    round once.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_up, b_up, w_down, b_down, offs, swiglu_alpha, swiglu_limit, store_aux):
+        if store_aux:
+            with timed("up_swiglu_fwd"):
+                s, aux = torch.ops.grouped_mm.mm_swiglu(x, w_up, offs, b_up, swiglu_alpha, swiglu_limit)
+        else:
+            with timed("up_swiglu_fwd"):
+                s = torch.ops.grouped_mm.mm_swiglu_noaux(x, w_up, offs, b_up, swiglu_alpha, swiglu_limit)
+            aux = None
+        with timed("down_fwd"):
+            out = torch.ops.grouped_mm.mm(s, w_down, offs, b_down, -1)
+        ctx.store_aux = bool(store_aux)
+        ctx.has_b_down = b_down is not None
+        ctx.alpha, ctx.limit = swiglu_alpha, swiglu_limit
+        ctx.save_for_backward(x, w_up, b_up, w_down, s, offs, *( [aux] if store_aux else []))
+        if b_down is not None:
+            ctx.b_down_shape, ctx.b_down_dtype = b_down.shape, b_down.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, w_up, b_up, w_down, s, offs = ctx.saved_tensors[:6]
+        need = ctx.needs_input_grad
+        need_x, need_wu, need_bu, need_wd, need_bd = need[0], need[1], need[2], need[3], need[4] and ctx.has_b_down
+        if not grad_out.numel():
+            z = lambda t, n: torch.zeros_like(t) if n else None  # noqa: E731
+            bd = torch.zeros(ctx.b_down_shape, dtype=ctx.b_down_dtype, device=x.device) if need_bd else None
+            return z(x, need_x), z(w_up, need_wu), z(b_up, need_bu), z(w_down, need_wd), bd, None, None, None, None
+        grad_out = grad_out.contiguous()
+        g_wd = g_bd = None
+        if need_wd and need_bd:
+            with timed("down_wgrad_bias"):
+                g_wd, g_bd = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), grad_out, offs)
+            g_bd = g_bd.to(ctx.b_down_dtype)
+        elif need_wd:
+            g_wd = torch.ops.grouped_mm.mm(s.transpose(-2, -1), grad_out, offs, None, -1)
+        elif need_bd:
+            g_bd = segment_sum_rows(grad_out, offs).to(ctx.b_down_dtype)
+        g_x = g_wu = g_bu = None
+        if need_x or need_wu or need_bu:
+            if ctx.store_aux:
+                aux = ctx.saved_tensors[6]
+            else:
+                with timed("up_recompute_aux"):
+                    aux = torch.ops.grouped_mm.mm(x, w_up, offs, b_up, -1)
+            with timed("down_dgrad_swiglu_bwd"):
+                grad_aux = torch.ops.grouped_mm.mm_swiglu_bwd(
+                    grad_out, w_down.transpose(-2, -1), offs, aux, ctx.alpha, ctx.limit
+                )
+            del aux
+            if need_x:
+                with timed("up_dgrad"):
+                    g_x = torch.ops.grouped_mm.mm(grad_aux, w_up.transpose(-2, -1), offs, None, -1)
+            if need_wu and need_bu:
+                with timed("up_wgrad_bias"):
+                    g_wu, g_bu = torch.ops.grouped_mm.mm_wgrad_bias(x.transpose(-2, -1), grad_aux, offs)
+                g_bu = g_bu.to(b_up.dtype)
+            elif need_wu:
+                g_wu = torch.ops.grouped_mm.mm(x.transpose(-2, -1), grad_aux, offs, None, -1)
+            elif need_bu:
+                g_bu = segment_sum_rows(grad_aux, offs).to(b_up.dtype)
+        return g_x, g_wu, g_bu, g_wd, g_bd, None, None, None, None
+
 
 # ============================================================================ EP row movement
 

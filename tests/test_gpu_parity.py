@@ -149,3 +149,30 @@ def test_config5_style_fine_grained_groups():
     got = _run_chain(x, w_up, b_up, w_down, b_down, offs, gout)
     ref = O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, gout)
     _compare_chain(got, ref, offs)
+
+
+@pytest.mark.parametrize("counts", [[70, 0, 131, 5], [0, 0, 0, 0], [256, 1, 0, 300]])
+def test_ffn_recompute_equals_stored_aux(counts):
+    """store_aux=False (aux recomputed in backward) gives the stored-aux results bit for bit, and both
+    match the oracle."""
+    from cutlass_op.bf16_grouped_mm import grouped_mm_ffn
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(4, 192, 96, counts, seed=sum(counts) + 1)
+    res = {}
+    for store_aux in (True, False):
+        leaves = [t.cuda().clone().requires_grad_(True) for t in (x, w_up, b_up, w_down, b_down)]
+        out = grouped_mm_ffn(leaves[0], leaves[1], leaves[3], offs.cuda(), leaves[2], leaves[4], store_aux=store_aux)
+        out.backward(gout.cuda())
+        torch.cuda.synchronize()
+        res[store_aux] = [out.detach()] + [t.grad for t in leaves]
+    _lib().check_device_status()
+    names = ["out", "dx", "dw_up", "db_up", "dw_down", "db_down"]
+    rows = int(offs[-1])
+    for name, a, b in zip(names, res[True], res[False]):
+        if name in ("out", "dx"):
+            a, b = a[:rows], b[:rows]
+        assert torch.equal(a, b), f"{name}: recompute differs from stored aux"
+    ref = O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, gout)
+    got = dict(zip(names, res[False]))
+    _compare_chain(got, ref, offs, keys=names)

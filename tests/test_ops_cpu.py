@@ -111,3 +111,21 @@ def test_config5_forced_group_sizes():
         assert int(c.sum()) == tokens * 8 and int(c.min()) >= 0
         for sz in (0, 1, 7, 129):
             assert sz in c.tolist()
+
+
+def test_recompute_path_shapes():
+    """store_aux=False: mm_swiglu_noaux returns swiglu_out only; the whole-FFN function runs its
+    forward on meta tensors with and without aux."""
+    from cutlass_op.bf16_grouped_mm import grouped_mm_ffn
+
+    _pkg()
+    assert "mm_swiglu_noaux(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha, " \
+           "float swiglu_limit) -> Tensor" in str(torch.ops.grouped_mm.mm_swiglu_noaux.default._schema)
+    E, H, I, M = 4, 256, 128, 300
+    x, wu, bu = _meta(M, H), _meta(E, H, 2 * I), _meta(E, 2 * I)
+    wd, bd = _meta(E, I, H), _meta(E, H)
+    offs = _meta(E, dtype=torch.int32)
+    s = torch.ops.grouped_mm.mm_swiglu_noaux(x, wu, offs, bu, 1.702, 7.0)
+    assert s.shape == (M, I)
+    for store_aux in (True, False):
+        assert grouped_mm_ffn(x, wu, wd, offs, bu, bd, store_aux=store_aux).shape == (M, H)
