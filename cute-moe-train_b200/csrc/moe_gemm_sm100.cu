@@ -82,6 +82,7 @@ struct Params {
   const int32_t* offs;
   const __nv_bfloat16* bias;
   int64_t bias_stride;
+  int bias_per_row;   // BIAS: bias[e, row - group start] added along the row
   __nv_bfloat16* d;
   int64_t ldd, ldd_batch;
   __nv_bfloat16* d2;
@@ -696,7 +697,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               float f[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-              if (p.bias != nullptr) {
+              if (EPI == MGF_EPI_BIAS && p.bias_per_row) {
+                const float bv = __bfloat162float(p.bias[(int64_t)ti.e * p.bias_stride + (grow - ti.row0 + ti.m_blk * TM)]);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) f[j] += bv;
+              } else if (p.bias != nullptr) {
                 const uint4* bp = reinterpret_cast<const uint4*>(p.bias + (int64_t)ti.e * p.bias_stride + col0);
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
@@ -1121,6 +1126,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.offs = g.offs;
   p.bias = static_cast<const __nv_bfloat16*>(g.bias);
   p.bias_stride = g.bias_stride;
+  p.bias_per_row = (g.epilogue == MGF_EPI_BIAS && g.bias != nullptr && g.bias_per_row) ? 1 : 0;
   p.d = static_cast<__nv_bfloat16*>(g.d);
   p.ldd = g.ldd;
   p.ldd_batch = g.ldd_batch;
@@ -1149,7 +1155,9 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   int bn, n_tiles, cg = 1;
   int64_t tiles_upper;
   if (!ragged_k) {
-    if (g.n <= 0 || g.k <= 0 || (g.n % 8) != 0 || (g.k % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
+    // k: any (TMA reads zeros past it; the row pitches carry the 16-byte rule); n: whole 16-byte
+    // output units
+    if (g.n <= 0 || g.k <= 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
     if (g.n > INT32_MAX || g.k > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
     if (!stride_ok(g.ldb_batch)) return MGF_ERR_ALIGNMENT;
     if (g.bias != nullptr && (!aligned16(g.bias) || !stride_ok(g.bias_stride))) return MGF_ERR_ALIGNMENT;
@@ -1186,7 +1194,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     }
     tiles_upper = (g.total_rows / (BM * cg) + g.num_groups) * static_cast<int64_t>(n_tiles);
   } else {
-    if (g.m <= 0 || g.n <= 0 || (g.m % 8) != 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
+    if (g.m <= 0 || g.n <= 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;  // m: any (A rows are 16-byte aligned by lda)
     if (g.m > INT32_MAX || g.n > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
     if (!stride_ok(g.ldd_batch)) return MGF_ERR_ALIGNMENT;
     if (g.d2 != nullptr && (!aligned16(g.d2) || !stride_ok(g.ldd2))) return MGF_ERR_ALIGNMENT;

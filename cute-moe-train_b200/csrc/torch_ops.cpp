@@ -87,7 +87,7 @@ int sm_carveout_for(const Tensor& t) {
 // Ragged-M launch: A [total_rows, k] row-major, B [E, k, n] (either major), D [total_rows, n].
 void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& offs, const Tensor* bias,
                      const Tensor& d, const Tensor* d2, const Tensor* aux, double alpha, double limit,
-                     bool store_aux, const char* what) {
+                     bool store_aux, const char* what, bool bias_per_row = false) {
   const bool b_col_major = check_strides_transposed(b, "mat_b");
   mgf_gemm_desc g = base_desc();
   g.epilogue = epi;
@@ -119,6 +119,7 @@ void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& of
   g.swiglu_alpha = static_cast<float>(alpha);
   g.swiglu_limit = static_cast<float>(limit);
   g.store_aux = store_aux ? 1 : 0;
+  g.bias_per_row = bias_per_row ? 1 : 0;
   g.sm_carveout = sm_carveout_for(a);
   check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
 }
@@ -161,6 +162,29 @@ std::tuple<Tensor, Tensor> ragged_k_launch(const Tensor& mat_a, const Tensor& ma
   return {out, db};
 }
 
+// Layout normalisation for the general `grouped_mm::mm` layouts the kernels do not read directly
+// (the reference's CUTLASS kernel takes row- and column-major A and B on every path,
+// csrc/grouped_mm_kernel.cuh:94-486).  These are explicit device copies into a layout the kernels
+// take, off the MoE hot path; the MoE layouts never copy.
+//
+// A copy of the last two dims of `t` in row-major order with the row pitch padded to 8 elements.
+Tensor row_major_padded(const Tensor& t) {
+  const int64_t r = t.size(-2), c = t.size(-1);
+  if (t.stride(-1) == 1 && t.stride(-2) % 8 == 0 && t.stride(-2) >= c &&
+      (t.dim() == 2 || t.stride(0) == r * t.stride(-2)) && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0)
+    return t;
+  std::vector<int64_t> sizes(t.sizes().begin(), t.sizes().end());
+  std::vector<int64_t> strides(t.dim());
+  strides[t.dim() - 1] = 1;
+  strides[t.dim() - 2] = padded(c);
+  if (t.dim() == 3) strides[0] = r * padded(c);
+  Tensor out = at::empty_strided(sizes, strides, t.options());
+  out.copy_(t);
+  return out;
+}
+// The same, column-major (a transposed view of a padded row-major copy of t^T).
+Tensor col_major_padded(const Tensor& t) { return row_major_padded(t.transpose(-2, -1)).transpose(-2, -1); }
+
 // ---------------------------------------------------------------- grouped_mm::mm
 Tensor mm_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::optional<Tensor>& offs,
                const std::optional<Tensor>& bias, int64_t out_dtype) {
@@ -186,36 +210,63 @@ Tensor mm_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::optional<Ten
   if (a2 && !b2) {
     // ragged-M: out [total_M, N]
     TORCH_CHECK(offs->size(0) == mat_b.size(0), "matrix batch sizes have to match");
-    TORCH_CHECK(!a_col, "grouped_mm: ragged-M with a column-major mat_a is not supported on this path");
+    const Tensor a = a_col ? row_major_padded(mat_a) : mat_a;
     const int64_t N = mat_b.size(2);
     if (bias.has_value()) check_bias(*bias, mat_b.size(0), N);
     Tensor out = at::empty_strided({mat_a.size(0), N}, {padded(N), 1}, mat_a.options());
-    launch_ragged_m(MGF_EPI_BIAS, mat_a, mat_b, *offs, bias.has_value() ? &*bias : nullptr, out, nullptr, nullptr,
+    launch_ragged_m(MGF_EPI_BIAS, a, mat_b, *offs, bias.has_value() ? &*bias : nullptr, out, nullptr, nullptr,
                     1.702, 7.0, false, "grouped_mm");
     return out;
   }
   if (a2 && b2) {
     TORCH_CHECK(!bias.has_value(), "grouped_mm: bias is not supported on the ragged-K path");
-    return std::get<0>(ragged_k_launch(mat_a, mat_b, *offs, false, "grouped_mm"));
+    // the kernel reads A as the transposed view of a row-major [total_K, M] and B row-major
+    const Tensor a = (mat_a.stride(0) == 1) ? mat_a : col_major_padded(mat_a);
+    const Tensor b = (mat_b.stride(1) == 1) ? mat_b : row_major_padded(mat_b);
+    return std::get<0>(ragged_k_launch(a, b, *offs, false, "grouped_mm"));
   }
   if (!a2 && !b2) {
     // batched: [B, M, K] x [B, K, N] -> [B, M, N]; run as ragged-M with equal groups.
     TORCH_CHECK(mat_a.size(0) == mat_b.size(0), "batched dimension has to match");
-    TORCH_CHECK(!a_col && mat_a.stride(0) == mat_a.size(1) * mat_a.stride(1),
-                "grouped_mm: batched mat_a must be row-major with packed batches on this path");
+    const Tensor a = row_major_padded(mat_a);
     const int64_t B = mat_a.size(0), M = mat_a.size(1), N = mat_b.size(2);
     if (bias.has_value()) check_bias(*bias, B, N);
     Tensor out = at::empty_strided({B, M, N}, {M * padded(N), padded(N), 1}, mat_a.options());
     TORCH_CHECK(B >= 1 && B <= 1024, "group count must be in [1, 1024]");
     Tensor boffs = at::arange(1, B + 1, mat_a.options().dtype(at::kInt)).mul_(static_cast<int>(M));
-    Tensor a_flat = mat_a.reshape({B * M, mat_a.size(2)});
+    Tensor a_flat = a.view({B * M, a.size(2)}).narrow(0, 0, B * M);
     Tensor out_flat = out.view({B * M, padded(N)}).narrow(1, 0, N);
     launch_ragged_m(MGF_EPI_BIAS, a_flat, mat_b, boffs, bias.has_value() ? &*bias : nullptr, out_flat, nullptr,
                     nullptr, 1.702, 7.0, false, "grouped_mm");
     return out;
   }
-  TORCH_CHECK(false, "grouped_mm: ragged-N (3D x 2D) is not supported on this path");
-  return Tensor();
+  // ragged-N: mat_a [E, M, K] x mat_b [K, total_N], groups along N (csrc/grouped_mm_common.cuh:107-118):
+  // out[:, cols(e)] = mat_a[e] @ mat_b[:, cols(e)] + bias[e, col - start(e)].  Run as the ragged-M
+  // GEMM of the transposed problem, out^T[cols(e), :] = mat_b^T[cols(e), :] @ mat_a[e]^T, whose bias is
+  // per row, then transposed into the row-major [M, total_N] output.
+  TORCH_CHECK(offs->size(0) == mat_a.size(0), "matrix batch sizes have to match");
+  const int64_t E = mat_a.size(0), M = mat_a.size(1), total_n = mat_b.size(1);
+  if (bias.has_value()) check_bias(*bias, E, total_n);
+  const Tensor at_rows = row_major_padded(mat_b.transpose(0, 1));  // [total_N, K]
+  // mat_a^T as B of the ragged-M GEMM: [E, K, M] (either major); M padded to a multiple of 8 with
+  // zero rows when needed so the kernel's n-extent stays in bounds
+  Tensor a3 = mat_a;
+  const int64_t Mp = padded(M);
+  if (Mp != M || !(mat_a.stride(-1) == 1 || mat_a.stride(-2) == 1)) {
+    a3 = at::zeros({E, Mp, mat_a.size(2)}, mat_a.options());
+    a3.narrow(1, 0, M).copy_(mat_a);
+  } else if (mat_a.stride(-1) == 1) {
+    a3 = row_major_padded(mat_a);
+  } else {
+    a3 = col_major_padded(mat_a);
+  }
+  const Tensor bt = a3.transpose(-2, -1);  // [E, K, Mp]
+  Tensor out_t = at::empty_strided({total_n, Mp}, {Mp, 1}, mat_a.options());
+  launch_ragged_m(MGF_EPI_BIAS, at_rows, bt, *offs, bias.has_value() ? &*bias : nullptr, out_t, nullptr, nullptr,
+                  1.702, 7.0, false, "grouped_mm", /*bias_per_row=*/true);
+  Tensor out = at::empty_strided({M, total_n}, {padded(total_n), 1}, mat_a.options());
+  out.copy_(out_t.narrow(1, 0, M).transpose(0, 1));
+  return out;
 }
 
 // ---------------------------------------------------------------- grouped_mm::mm_swiglu
@@ -316,7 +367,9 @@ std::tuple<Tensor, Tensor> mm_wgrad_bias_cuda(const Tensor& mat_a, const Tensor&
   check_strides_transposed(mat_a, "mat_a");
   check_strides_transposed(mat_b, "mat_b");
   check_offs(offs, mat_a);
-  return ragged_k_launch(mat_a, mat_b, offs, true, "grouped_mm_wgrad_bias");
+  const Tensor a = (mat_a.stride(0) == 1) ? mat_a : col_major_padded(mat_a);
+  const Tensor b = (mat_b.stride(1) == 1) ? mat_b : row_major_padded(mat_b);
+  return ragged_k_launch(a, b, offs, true, "grouped_mm_wgrad_bias");
 }
 
 // ---------------------------------------------------------------- expert-parallel row movement

@@ -104,6 +104,22 @@ def segment_sum_rows(grad: torch.Tensor, offs: torch.Tensor) -> torch.Tensor:
     return acc.to(grad.dtype)
 
 
+def segment_sum_cols(grad: torch.Tensor, offs: torch.Tensor) -> torch.Tensor:
+    """Bias gradient of the ragged-N layout (custom_op.py:104-131): column sums of ``grad`` [M, total_N]
+    in fp32, placed at [group, column - group start] of an [E, total_N] result."""
+    groups = offs.numel()
+    total_n = grad.shape[1]
+    col_sum = grad.sum(dim=0, dtype=torch.float32)
+    cols = torch.arange(total_n, device=grad.device, dtype=torch.int64)
+    ends = offs.to(torch.int64)
+    gid = torch.bucketize(cols, ends, right=True)
+    starts = torch.cat([ends.new_zeros(1), ends[:-1]])
+    keep = gid < groups  # columns past offs[-1] belong to no group
+    acc = torch.zeros((groups, total_n), dtype=torch.float32, device=grad.device)
+    acc[gid[keep], cols[keep] - starts[gid[keep]]] = col_sum[keep]
+    return acc.to(grad.dtype)
+
+
 def _is_col_major(t: torch.Tensor) -> bool:
     d = t.dim()
     return t.stride(d - 2) == 1 and t.stride(d - 1) == t.size(d - 2)
@@ -180,7 +196,13 @@ def _mm_backward(ctx, grad_out):
         if need_bias:
             gbias = grad_out.sum(dim=-2, dtype=torch.float32).to(grad_out.dtype)
     else:
-        raise RuntimeError("grouped_mm: ragged-N (3D x 2D) is not supported on this path")
+        # ragged-N: out[:, cols(e)] = a[e] @ b[:, cols(e)] (+ bias[e, local col]), custom_op.py:263-330
+        if need_a:
+            ga = torch.ops.grouped_mm.mm(grad_out, mat_b.transpose(-2, -1), offs, None, -1)
+        if need_b:
+            gb = torch.ops.grouped_mm.mm(mat_a.transpose(-2, -1), grad_out, offs, None, -1)
+        if need_bias:
+            gbias = segment_sum_cols(grad_out, offs).to(ctx.bias_dtype)
     return ga, gb, None, gbias, None
 
 

@@ -72,6 +72,9 @@ enum mgf_status {
  *   B    : [total_rows, n] row-major (stride ldb).
  *   D    : [E, m, n] bf16, row stride ldd, batch stride ldd_batch.  Empty groups get zeros.
  *   D2   : optional [E, n] bf16 bias gradient (stride ldd2 between groups): column sums of B.
+ * Extents: n a multiple of 8 (whole 16-byte output units); k (ragged-M) and m (ragged-K) any
+ * positive value.  Every base pointer 16-byte aligned and every row / batch stride a multiple of
+ * 8 elements (the TMA rule); reads past k, m, n or total_rows return zeros.
  */
 typedef struct mgf_gemm_desc {
   int32_t epilogue;      /* enum mgf_epilogue */
@@ -102,6 +105,9 @@ typedef struct mgf_gemm_desc {
                             counter (tiles of a ragged-K launch cost in proportion to their group's
                             size; handing them out in order keeps the CTAs on neighbouring tiles).
                             NULL = static tile striding.  One workspace per launch in flight. */
+  int32_t bias_per_row;  /* BIAS, ragged-M only: 0 = bias[e, col] added to every row (the MoE case);
+                            1 = bias[e, row - group start] added to every column of a row (the
+                            transposed form of the reference's ragged-N bias, csrc/grouped_mm_common.cuh:107-118) */
 } mgf_gemm_desc;
 
 /* Launch one grouped GEMM on `stream` (a cudaStream_t; NULL = legacy default stream).

@@ -129,3 +129,24 @@ def test_recompute_path_shapes():
     assert s.shape == (M, I)
     for store_aux in (True, False):
         assert grouped_mm_ffn(x, wu, wd, offs, bu, bd, store_aux=store_aux).shape == (M, H)
+
+
+def test_segment_sum_cols_groups_columns_like_the_forward():
+    """Ragged-N bias gradient: column c of group e (start(e) <= c < end(e)) lands at [e, c - start(e)];
+    columns past offs[-1] belong to no group."""
+    from cutlass_op.bf16_grouped_mm.custom_op import segment_sum_cols
+
+    g = torch.randn(5, 10)
+    offs = torch.tensor([3, 3, 8], dtype=torch.int32)
+    got = segment_sum_cols(g, offs)
+    ref = torch.zeros(3, 10)
+    ref[0, :3] = g[:, 0:3].sum(0)
+    ref[2, :5] = g[:, 3:8].sum(0)
+    assert torch.allclose(got, ref, atol=1e-6)
+
+
+def test_fake_shape_ragged_n():
+    m = _pkg()
+    offs = _meta(3, dtype=torch.int32)
+    out = m.grouped_mm(_meta(3, 72, 64), _meta(64, 208), offs)
+    assert out.shape == (72, 208)
