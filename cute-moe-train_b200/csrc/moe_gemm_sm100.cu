@@ -1055,7 +1055,9 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace mgf;
 
-extern "C" int mgf_version(void) { return 100; }
+extern "C" int mgf_version(void) { return 101; }
+
+extern "C" size_t mgf_gemm_desc_size(void) { return sizeof(mgf_gemm_desc); }
 
 extern "C" const char* mgf_last_error_detail(void) { return g_last_error; }
 

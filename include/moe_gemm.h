@@ -26,6 +26,7 @@
 #ifndef MOE_GEMM_H_
 #define MOE_GEMM_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -173,6 +174,10 @@ const char* mgf_last_error_detail(void);
 
 /* Library ABI version (major * 100 + minor). */
 int mgf_version(void);
+
+/* sizeof(mgf_gemm_desc) as compiled into the library, for bindings that declare the struct
+ * themselves (ctypes, cffi) to check their layout against. */
+size_t mgf_gemm_desc_size(void);
 
 #ifdef __cplusplus
 }

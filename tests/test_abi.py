@@ -40,3 +40,22 @@ def test_status_strings_and_version():
 def test_null_descriptor_rejected():
     lib = ctypes.CDLL(str(LIB))
     assert lib.mgf_grouped_gemm_launch(None, None) == -1
+
+
+def test_ctypes_descriptor_layouts_match_the_library():
+    """The ctypes mirrors of mgf_gemm_desc (the INTEGRATION stub and the no-alloc test's) have the
+    size the library was compiled with."""
+    import importlib.util
+
+    lib = ctypes.CDLL(str(LIB))
+    lib.mgf_gemm_desc_size.restype = ctypes.c_size_t
+    spec = importlib.util.spec_from_file_location("t_no_alloc", REPO / "tests" / "test_zz_no_alloc.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert ctypes.sizeof(mod.MgfGemmDesc) == lib.mgf_gemm_desc_size()
+    stub = (REPO / "INTEGRATION.md").read_text()
+    block = stub[stub.index("class MgfGemmDesc(ctypes.Structure):"):]
+    block = block[: block.index("\n\n")]
+    ns = {"ctypes": ctypes}
+    exec(block, ns)  # the documented stub, as a maintainer would paste it
+    assert ctypes.sizeof(ns["MgfGemmDesc"]) == lib.mgf_gemm_desc_size()
