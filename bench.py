@@ -53,6 +53,8 @@ def parse_args():
                     help="cfg3 (1 GPU) / cfg4 (EP) by default; cfg2 = forward only; cfg5 = E=256 fine-grained")
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="uniform",
                     help="expert-parallel routing (cfg4 lists both; uniform is the balanced case)")
+    ap.add_argument("--ep-overlap", action="store_true",
+                    help="peer transport: push the dispatch gradient under the up-proj weight gradient")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
@@ -167,7 +169,8 @@ def build_workload(args, rank, world, device):
     E_total = args.experts or 128
     desc = (f"cfg4: GPT-OSS-120B experts E=128 H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
             f"expert parallel E/{world} per GPU, dispatch/combine by "
-            + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all"))
+            + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all")
+            + (", dispatch gradient pushed under the up-proj wgrad" if args.ep_overlap else ""))
     return wl, desc, E_total, 0, tokens, topk, H, I, 1.1, False
 
 
@@ -322,7 +325,8 @@ def main():
     else:
         from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
-        ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport)
+        ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport,
+                       overlap=args.ep_overlap)
         gx = torch.Generator(device=device).manual_seed(1 + rank)
         x = torch.randn(tokens, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
         expert_idx = route_tokens(tokens, E_total, topk, args.routing, seed=100 + rank, device=device)

@@ -307,6 +307,7 @@ class PeerBuffers:
                 ptrs.append(self._opened[handle] + offset)
             self.bases[k] = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self.side_stream = torch.cuda.Stream(device=device)
 
     def close(self):
         from ._ext import ipc_close
@@ -341,13 +342,74 @@ class _PeerDispatch(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_rows):
         st = ctx.st
-        with timed("ep_peer_dispatch_bwd"):
-            torch.ops.grouped_mm.push_rows(g_rows.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
-                                           st.plan["src_pos"], st.bufs.bases["gret"], st.n, g_rows.shape[1], st.cap)
-        st.bufs.barrier()
+        if getattr(st, "dispatch_bwd_done", None) is not None:
+            # already pushed (and the barrier passed) on the side stream by the expert FFN's backward
+            torch.cuda.current_stream().wait_event(st.dispatch_bwd_done)
+            st.dispatch_bwd_done = None
+        else:
+            _push_rows_grad(g_rows, st)
+            st.bufs.barrier()
         with timed("ep_combine"):
             gx = torch.ops.grouped_mm.combine_rows(st.bufs.local["gret"], st.inv_order, None, st.k)
         return gx, None
+
+
+def _push_rows_grad(g_rows: torch.Tensor, st) -> None:
+    """Gradient of the dispatch: each received row's gradient goes back to its source's `gret`."""
+    with timed("ep_peer_dispatch_bwd"):
+        torch.ops.grouped_mm.push_rows(g_rows.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
+                                       st.plan["src_pos"], st.bufs.bases["gret"], st.n, g_rows.shape[1], st.cap)
+
+
+def _start_dispatch_bwd(g_rows: torch.Tensor, st) -> None:
+    """Push the rows' gradient and pass the barrier on the side stream, so both run under the
+    up-projection weight gradient that the expert FFN's backward launches next; the dispatch's
+    backward then only waits for the recorded event."""
+    side = st.side_stream
+    side.wait_stream(torch.cuda.current_stream())
+    g_rows.record_stream(side)
+    with torch.cuda.stream(side):
+        _push_rows_grad(g_rows, st)
+        st.bufs.barrier()
+        ev = torch.cuda.Event()
+        ev.record(side)
+    st.dispatch_bwd_done = ev
+
+
+class _EPExpertFFN(torch.autograd.Function):
+    """The local experts' fused FFN (grouped_mm_swiglu -> grouped_mm_downproj) for the peer transport.
+
+    Same launches and results as the two wrappers; the backward hands the received rows' gradient
+    to the dispatch push on a side stream as soon as the up-projection dgrad has produced it, before
+    launching the up-projection weight gradient, so the NVLink push and its barrier overlap that GEMM
+    (the push kernel's blocks co-reside with the GEMM's one CTA per SM).
+    """
+
+    @staticmethod
+    def forward(ctx, rows, w_up, b_up, w_down, b_down, offs, alpha, limit, st):
+        with timed("up_swiglu_fwd"):
+            s, aux = torch.ops.grouped_mm.mm_swiglu(rows, w_up, offs, b_up, alpha, limit)
+        with timed("down_fwd"):
+            y = torch.ops.grouped_mm.mm(s, w_down, offs, b_down, -1)
+        ctx.save_for_backward(rows, w_up, w_down, s, aux, offs)
+        ctx.alpha, ctx.limit, ctx.st = alpha, limit, st
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        rows, w_up, w_down, s, aux, offs = ctx.saved_tensors
+        g = g.contiguous()
+        with timed("down_wgrad_bias"):
+            g_wd, g_bd = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), g, offs)
+        with timed("down_dgrad_swiglu_bwd"):
+            grad_aux = torch.ops.grouped_mm.mm_swiglu_bwd(g, w_down.transpose(-2, -1), offs, aux, ctx.alpha, ctx.limit)
+        with timed("up_dgrad"):
+            g_rows = torch.ops.grouped_mm.mm(grad_aux, w_up.transpose(-2, -1), offs, None, -1)
+        if ctx.needs_input_grad[0] and ctx.st.overlap:
+            _start_dispatch_bwd(g_rows, ctx.st)
+        with timed("up_wgrad_bias"):
+            g_wu, g_bu = torch.ops.grouped_mm.mm_wgrad_bias(rows.transpose(-2, -1), grad_aux, offs)
+        return g_rows, g_wu, g_bu.to(w_up.dtype), g_wd, g_bd.to(w_down.dtype), None, None, None, None
 
 
 class _PeerCombine(torch.autograd.Function):
@@ -382,7 +444,8 @@ class _PeerCombine(torch.autograd.Function):
 
 
 def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
-                    bufs_cache: dict, group=None, router_weights: torch.Tensor | None = None) -> tuple:
+                    bufs_cache: dict, group=None, router_weights: torch.Tensor | None = None,
+                    overlap: bool = False) -> tuple:
     """Expert-parallel MoE FFN with dispatch/combine as peer-memory pushes (CUDA, world > 1).
 
     Same contract as ep_moe_ffn.  Every rank must pass the same number of tokens.  The receive buffers
@@ -418,8 +481,12 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
         dist.all_gather_into_tensor(c_all, counts, group=group)
         st.plan = push_plan(c_all, flat[st.order], rank, world, e_local, cap)
     st.bufs, st.k, st.n, st.cap = bufs, k, n, cap
+    st.side_stream = bufs.side_stream
+    st.dispatch_bwd_done = None
+    st.overlap = overlap
     rows = _PeerDispatch.apply(x, st)
-    y = expert_fn(rows, st.plan["offs"])
+    y = expert_fn(rows, st.plan["offs"], st) if getattr(expert_fn, "takes_peer_state", False) else \
+        expert_fn(rows, st.plan["offs"])
     w_flat = router_weights.reshape(-1).float().contiguous() if router_weights is not None else None
     out = _PeerCombine.apply(y, w_flat, st)
     bufs.pending_backward = out.requires_grad
@@ -432,8 +499,13 @@ class EPMoEFFN(torch.nn.Module):
     """GPT-OSS-style MoE FFN whose E experts are sharded E/N per rank, run with the fused kernels."""
 
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
-                 swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer"):
+                 swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer",
+                 overlap: bool = False):
+        """transport: "peer" (NVLink pushes, CUDA, world > 1) or "nccl" (all-to-all).  overlap (peer
+        transport): push the dispatch's gradient on a side stream under the up-projection weight
+        gradient instead of after it."""
         super().__init__()
+        self.overlap = overlap
         if transport not in ("peer", "nccl"):
             raise ValueError(f"transport must be 'peer' or 'nccl', got {transport!r}")
         self.transport = transport
@@ -461,11 +533,17 @@ class EPMoEFFN(torch.nn.Module):
         s, aux = grouped_mm_swiglu(rows, self.w_up, offs, self.b_up, self.alpha, self.limit)
         return grouped_mm_downproj(s, self.w_down, offs, self.b_down, aux, self.alpha, self.limit)
 
+    def _peer_expert_fn(self, rows: torch.Tensor, offs: torch.Tensor, st) -> torch.Tensor:
+        return _EPExpertFFN.apply(rows, self.w_up, self.b_up, self.w_down, self.b_down, offs, self.alpha,
+                                  self.limit, st)
+
+    _peer_expert_fn.takes_peer_state = True
+
     def forward(self, x: torch.Tensor, expert_idx: torch.Tensor, router_weights: torch.Tensor | None = None):
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if self.transport == "peer" and world > 1 and x.is_cuda:
-            out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self.expert_fn, self._peer_bufs, self.group,
-                                      router_weights)
+            out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self._peer_expert_fn, self._peer_bufs,
+                                      self.group, router_weights, overlap=self.overlap)
             self.last_local_rows = st.plan["n_recv"]  # device tensor; read it outside timed regions
             return out
         out, plan = ep_moe_ffn(x, expert_idx, self.num_experts, self.expert_fn, self.group, router_weights)
