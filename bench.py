@@ -176,7 +176,9 @@ def build_workload(args, rank, world, device):
 
 # ------------------------------------------------------------------------------------- runs
 
-def time_steps(step_fn, steps, warmup, barrier=None, sync=None):
+def time_steps(step_fn, steps, warmup, barrier=None, sync=None, tail=None):
+    """Device time per step.  `tail` runs after the last step, inside the timed window (work the
+    steps issued on other streams that must be counted)."""
     import torch
 
     for _ in range(warmup):
@@ -189,6 +191,8 @@ def time_steps(step_fn, steps, warmup, barrier=None, sync=None):
     a.record()
     for _ in range(steps):
         step_fn()
+    if tail:
+        tail()
     b.record()
     torch.cuda.synchronize()
     if barrier:
@@ -467,37 +471,64 @@ def compare_torch(step_inputs, steps, warmup, flops, fwd_only=False):
 
 
 def e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops, fwd_only=False):
-    """Public-API step with the step's inputs copied from pinned host memory and the loss read back."""
+    """Public-API step with the step's inputs copied from pinned host memory and the loss read back.
+
+    Every step copies its x rows and offs host -> device and reads the loss device -> host.  The
+    copies run on a copy stream into the other of two device buffers while the previous step
+    computes (a data prefetcher), and the timed window ends only after the last of them has landed:
+    K timed steps hold K full host -> device copies and K fwd+bwd passes.
+    """
     import torch
 
     x_host = x.detach().to("cpu").pin_memory()
     offs_host = offs.to("cpu").pin_memory()
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-    x_dev = torch.empty_like(x.detach())
-    offs_dev = torch.empty_like(offs)
+    x_dev = [torch.empty_like(x.detach()) for _ in range(2)]
+    offs_dev = [torch.empty_like(offs) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    copy_stream = torch.cuda.Stream()
     params = [w_up, b_up, w_down, b_down]
+    state = {"i": 0}
+
+    def issue_copy(slot):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[slot])  # the step that last read this buffer is done
+            x_dev[slot].copy_(x_host, non_blocking=True)
+            offs_dev[slot].copy_(offs_host, non_blocking=True)
+            ready[slot].record(copy_stream)
+
+    issue_copy(0)
 
     def step():
+        slot = state["i"] & 1
+        state["i"] += 1
+        issue_copy(slot ^ 1)  # the next step's inputs, under this step's compute
+        torch.cuda.current_stream().wait_event(ready[slot])
         for p in params:
             p.grad = None
-        x_dev.copy_(x_host, non_blocking=True)
-        offs_dev.copy_(offs_host, non_blocking=True)
+        xs, os_ = x_dev[slot], offs_dev[slot]
         if fwd_only:
             with torch.no_grad():
-                s, _ = mgf.grouped_mm_swiglu(x_dev, w_up, offs_dev, b_up, ALPHA, LIMIT)
-                loss_host.copy_(s.float().sum(), non_blocking=True)
-            return
-        xl = x_dev.detach().requires_grad_(True)
-        s, aux = mgf.grouped_mm_swiglu(xl, w_up, offs_dev, b_up, ALPHA, LIMIT)
-        out = mgf.grouped_mm_downproj(s, w_down, offs_dev, b_down, aux, ALPHA, LIMIT)
-        loss = out.float().sum()
-        loss.backward()
-        loss_host.copy_(loss.detach(), non_blocking=True)
+                s, _ = mgf.grouped_mm_swiglu(xs, w_up, os_, b_up, ALPHA, LIMIT)
+                loss_host.copy_(s.sum(dtype=torch.float32), non_blocking=True)
+        else:
+            xl = xs.detach().requires_grad_(True)
+            s, aux = mgf.grouped_mm_swiglu(xl, w_up, os_, b_up, ALPHA, LIMIT)
+            out = mgf.grouped_mm_downproj(s, w_down, os_, b_down, aux, ALPHA, LIMIT)
+            loss = out.sum(dtype=torch.float32)
+            loss.backward()
+            loss_host.copy_(loss.detach(), non_blocking=True)
+        free[slot].record()
 
-    ms = time_steps(step, args.steps, args.warmup)
+    def tail():
+        torch.cuda.current_stream().wait_stream(copy_stream)
+
+    ms = time_steps(step, args.steps, args.warmup, tail=tail)
     return {"value": flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
             "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + offs_host.numel() * 4,
-            "d2h_bytes_per_step": 4}
+            "d2h_bytes_per_step": 4,
+            "h2d": "pinned host -> device on a copy stream, one step ahead (double-buffered prefetch)"}
 
 
 if __name__ == "__main__":

@@ -179,8 +179,9 @@ def _transport_worker(rank, world, port, q):
             from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
             res = {}
-            for transport in ("nccl", "peer"):
-                ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport)
+            for transport in ("nccl", "peer", "peer_overlap"):
+                ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport.split("_")[0],
+                               overlap=transport.endswith("overlap"))
                 x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
                 x = x.to(dev).requires_grad_(True)
                 idx = route_tokens(T, E, K, "zipf", seed=20 + rank).to(dev)
@@ -205,7 +206,8 @@ def _transport_worker(rank, world, port, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_world2_peer_transport_matches_nccl():
-    """Dispatch/combine as peer-memory pushes gives the NCCL all-to-all path's outputs and gradients."""
+    """Dispatch/combine as peer-memory pushes gives the NCCL all-to-all path's outputs and gradients;
+    with the dispatch-gradient push overlapped, bit-identical ones."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -230,3 +232,6 @@ def test_ep_world2_peer_transport_matches_nccl():
         for name, a, b in zip(names, res[rank]["peer"], res[rank]["nccl"]):
             r = O.check(f"rank{rank}:{name}", torch.from_numpy(a), torch.from_numpy(b))
             assert r["ok"], r
+        # the overlapped dispatch-gradient push changes the timing, not one bit of the results
+        for name, a, b in zip(names, res[rank]["peer_overlap"], res[rank]["peer"]):
+            assert (a == b).all(), f"rank{rank}:{name}: overlap changed the result"
