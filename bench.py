@@ -39,7 +39,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # FLOPs of each operator per launch, in units of M*H*I (M routed rows on this GPU).
 OP_FLOP_UNITS = {
     "up_swiglu_fwd": 4, "down_fwd": 2, "down_wgrad_bias": 2, "down_dgrad_swiglu_bwd": 2,
-    "up_dgrad": 4, "up_wgrad_bias": 4, "up_recompute_aux": 4,
+    "up_dgrad": 4, "up_wgrad_bias": 4, "up_recompute_aux": 4, "fp8_up_swiglu_fwd": 4,
 }
 
 
@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
+    ap.add_argument("--fp8", action="store_true",
+                    help="cfg2 only: the e4m3 up-projection + SwiGLU (row-wise scales; inputs quantised "
+                         "before the timed region)")
     ap.add_argument("--recompute-aux", action="store_true",
                     help="store_aux=False: the forward keeps no aux, the backward recomputes it "
                          "(the extra GEMM's FLOPs are not counted in the metric)")
@@ -311,13 +314,24 @@ def main():
         w_up, b_up, w_down, b_down = [t.requires_grad_(True) for t in
                                       make_weights_device(MoEShape(E, H, I), seed=2, device=device)]
         params = [x, w_up, b_up, w_down, b_down]
+        if args.fp8:
+            if not fwd_only:
+                raise SystemExit("--fp8 needs --workload cfg2 (the FP8 operators are forward-only)")
+            from cutlass_op.bf16_grouped_mm import fp8 as fp8_mod
+
+            with torch.no_grad():
+                qx, sx = fp8_mod.quantize_rows(x.detach())
+                qw, sw = fp8_mod.quantize_weights(w_up.detach())
 
         def step():
             for p in params:
                 p.grad = None
             if fwd_only:
                 with torch.no_grad():
-                    mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
+                    if args.fp8:
+                        fp8_mod.grouped_mm_swiglu_fp8(qx, qw, offs, sx, sw, b_up, ALPHA, LIMIT)
+                    else:
+                        mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
                 return
             if args.recompute_aux:
                 out = mgf.grouped_mm_ffn(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT, store_aux=False)
@@ -382,10 +396,13 @@ def main():
         fl = OP_FLOP_UNITS[name] * float(local_rows) * H * I
         ach = fl / (ops[name]["avg_ms"] * 1e-3) / 1e12
         peak = peaks["bf16_tflops_sustained"]
+        peak_name = f"{peak_src} bf16_tflops_sustained"
+        if args.fp8:  # no measured e4m3 peak on this pool: the nominal dense figure
+            peak, peak_name = 4500.0, "nominal e4m3 dense 4.5 PFLOP/s (no measured fp8 peak)"
         traffic = load_traffic()
         roof = {"bound": "tensor", "kernel": name, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                "frac": ach / peak, "peak_source": f"{peak_src} bf16_tflops_sustained",
-                "traffic": (traffic or {}).get("bytes_per_launch"),
+                "frac": ach / peak, "peak_source": peak_name,
+                "traffic": (traffic or {}).get("bytes_per_launch") if (traffic or {}).get("op") == name else None,
                 "algorithmic_flop_per_launch": fl,
                 "ops": {k: {"avg_ms": round(v["avg_ms"], 4), "launches": v["launches"],
                             "tflops": OP_FLOP_UNITS.get(k, 0) * float(local_rows) * H * I / (v["avg_ms"] * 1e-3) / 1e12}
@@ -394,11 +411,14 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, shapes of the configured workload)",
+        "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out" if args.fp8 else "bf16",
+        "data": "synthetic (seeded, shapes of the configured workload)",
         "config": {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
                    "routed_rows_gpu0": local_rows, "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (x 566 MB + weights >= 1.6 GB per GPU), no flush",
-                   "step": ("grouped_mm_swiglu forward only (config 2)" if fwd_only else
+                   "step": (("grouped_mm_swiglu_fp8 forward only (config 2 shapes, row-wise e4m3 inputs "
+                             "quantised before the timed region)" if args.fp8 else
+                             "grouped_mm_swiglu forward only (config 2)") if fwd_only else
                             "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
                             "(the metric is the MoE FFN fwd+bwd)"
                             + ("; store_aux=False: aux recomputed in backward, 18*M*H*I FLOPs counted"

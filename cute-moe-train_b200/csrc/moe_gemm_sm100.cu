@@ -83,6 +83,10 @@ struct Params {
   const __nv_bfloat16* bias;
   int64_t bias_stride;
   int bias_per_row;   // BIAS: bias[e, row - group start] added along the row
+  int bke;            // elements of K per pipeline stage (64 bf16 or 128 e4m3: 128 bytes)
+  const float* scale_a;  // e4m3: per-row scale of A
+  const float* scale_b;  // e4m3: per-(group, column) scale of B
+  int64_t scale_b_stride;
   __nv_bfloat16* d;
   int64_t ldd, ldd_batch;
   __nv_bfloat16* d2;
@@ -205,7 +209,7 @@ __device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedS
     ti.row_end = s.seg_end[lo];
     ti.k_start = 0;
     ti.k_end = p.k;
-    ti.nk = (p.k + BK - 1) / BK;
+    ti.nk = (p.k + p.bke - 1) / p.bke;
   } else {
     ti.row0 = 0;
     ti.row_end = 0;
@@ -320,7 +324,7 @@ __device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, i
 // Stages whose odd-CTA half must be patched first (ragged-K tails, the ones row) are "relayed":
 // the odd CTA counts their bytes on its own barrier, patches, then arrives on the even CTA's
 // patch_done barrier; every other stage counts both CTAs' bytes directly on the even CTA's barrier.
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const Params p) {
@@ -490,12 +494,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             else ptx::tma_load_3d(dst, tm, fb, x, y, z);
           };
           if constexpr (!RAGGED_K) {
-            load2(sA, &tmA, kb * BK, ti.row0 + static_cast<int>(crank) * BM);
+            constexpr int BKE = F8 ? 128 : BK;  // K elements per stage (128 bytes of a row)
+            load2(sA, &tmA, kb * BKE, ti.row0 + static_cast<int>(crank) * BM);
             if constexpr (B_MN) {
 #pragma unroll
               for (int c = 0; c < Cfg::B_CHUNKS; ++c) load3(sB + c * 8192, &tmB, nb0 + 64 * c, kb * BK, ti.e);
             } else {
-              load3(sB, &tmB, kb * BK, nb0, ti.e);
+              load3(sB, &tmB, kb * BKE, nb0, ti.e);
             }
           } else {
             const int kr = ti.k_start + kb * BK;
@@ -530,7 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (even CTA) /
     //                                                              ragged-K stage patcher (odd CTA)
-    constexpr uint32_t idesc = ptx::make_idesc_bf16(TM, BN, A_MN, B_MN);
+    constexpr uint32_t idesc =
+        F8 ? ptx::make_idesc_e4m3(TM, BN, A_MN, B_MN) : ptx::make_idesc_bf16(TM, BN, A_MN, B_MN);
     constexpr uint32_t a_lbo = A_MN ? 8192u : 16u;
     constexpr uint32_t b_lbo = B_MN ? 8192u : 16u;
     constexpr uint32_t a_kstep = A_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
@@ -613,8 +619,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            if constexpr (CG == 2) {
+            // one instruction consumes 32 bytes of every K-major row: K = 16 bf16 or K = 32 e4m3
+            if constexpr (CG == 2 && F8) {
+              ptx::umma_f8_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+            } else if constexpr (CG == 2) {
               ptx::umma_bf16_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+            } else if constexpr (F8) {
+              ptx::umma_f8(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             } else {
               ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             }
@@ -697,6 +708,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               float f[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+              if constexpr (F8) {
+                // dequantise: row scale of A times the group's column scales of B (fp32), then bias
+                const float sa = __ldg(p.scale_a + grow);
+                const float4* sp = reinterpret_cast<const float4*>(p.scale_b + (int64_t)ti.e * p.scale_b_stride + col0);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  if (col0 + 4 * g < p.n) {
+                    const float4 sb = __ldg(sp + g);
+                    f[4 * g] *= sa * sb.x;
+                    f[4 * g + 1] *= sa * sb.y;
+                    f[4 * g + 2] *= sa * sb.z;
+                    f[4 * g + 3] *= sa * sb.w;
+                  }
+                }
+              }
               if (EPI == MGF_EPI_BIAS && p.bias_per_row) {
                 const float bv = __bfloat162float(p.bias[(int64_t)ti.e * p.bias_stride + (grow - ti.row0 + ti.m_blk * TM)]);
 #pragma unroll
@@ -870,7 +896,8 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                        const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                        const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B,
+                        CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = get_encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t d[3];
@@ -882,7 +909,7 @@ static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64
     b[i] = box[i];
   }
   for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
-  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
+  const CUresult r = fn(m, dtype, rank, const_cast<void*>(base), d, s, b, e,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -922,11 +949,11 @@ static bool debug_sync() {
   return v == 1;
 }
 
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false>
 static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD, const Params& p,
                        int grid_in, cudaStream_t st) {
   int grid = grid_in;
-  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG>;
+  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG, F8>;
   constexpr int smem = TileCfg<BN, CG, B_MN>::SMEM_BYTES;
   static std::mutex mu;
   static bool attr_done[64] = {};
@@ -992,8 +1019,14 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUten
 }
 
 template <int BN, int CG>
-static int dispatch_epi(int epi, bool b_mn, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD,
-                        const Params& p, int grid, cudaStream_t st) {
+static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, const CUtensorMap& tB,
+                        const CUtensorMap& tD, const Params& p, int grid, cudaStream_t st) {
+  if (f8) {  // e4m3: ragged-M forward epilogues, both operands K-major
+    if (b_mn) return MGF_ERR_INVALID_ARGUMENT;
+    if (epi == MGF_EPI_BIAS) return launch_inst<BN, MGF_EPI_BIAS, false, false, CG, true>(tA, tB, tD, p, grid, st);
+    if (epi == MGF_EPI_SWIGLU) return launch_inst<BN, MGF_EPI_SWIGLU, false, false, CG, true>(tA, tB, tD, p, grid, st);
+    return MGF_ERR_INVALID_ARGUMENT;
+  }
   switch (epi) {
     case MGF_EPI_BIAS:
       return b_mn ? launch_inst<BN, MGF_EPI_BIAS, false, true, CG>(tA, tB, tD, p, grid, st)
@@ -1151,7 +1184,21 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   auto stride_ok = [](int64_t s) { return s > 0 && (s % 8) == 0; };
   if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.d)) return MGF_ERR_ALIGNMENT;
   if (!stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
-  if (!no_rows && (!stride_ok(g.lda) || !stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
+  const bool f8 = g.ab_type == MGF_AB_E4M3;
+  if (g.ab_type != MGF_AB_BF16 && !f8) return MGF_ERR_INVALID_ARGUMENT;
+  const int esz = f8 ? 1 : 2;  // bytes per A / B element
+  auto ab_stride_ok = [esz](int64_t s) { return s > 0 && (s * esz) % 16 == 0; };
+  if (!no_rows && (!ab_stride_ok(g.lda) || !ab_stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
+  if (f8) {
+    if (ragged_k || g.b_mn_major || (g.epilogue != MGF_EPI_BIAS && g.epilogue != MGF_EPI_SWIGLU) ||
+        g.scale_a == nullptr || g.scale_b == nullptr || g.bias_per_row)
+      return MGF_ERR_INVALID_ARGUMENT;
+    if (!aligned16(g.scale_b) || (g.scale_b_stride % 4) != 0 || g.scale_b_stride < 0) return MGF_ERR_ALIGNMENT;
+  }
+  p.bke = f8 ? 128 : BK;
+  p.scale_a = g.scale_a;
+  p.scale_b = g.scale_b;
+  p.scale_b_stride = g.scale_b_stride;
 
   CUtensorMap tA, tB, tD;
   int bn, n_tiles, cg = 1;
@@ -1161,7 +1208,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     // output units
     if (g.n <= 0 || g.k <= 0 || (g.n % 8) != 0) return MGF_ERR_INVALID_ARGUMENT;
     if (g.n > INT32_MAX || g.k > INT32_MAX) return MGF_ERR_INVALID_ARGUMENT;
-    if (!stride_ok(g.ldb_batch)) return MGF_ERR_ALIGNMENT;
+    if (!ab_stride_ok(g.ldb_batch)) return MGF_ERR_ALIGNMENT;
     if (g.bias != nullptr && (!aligned16(g.bias) || !stride_ok(g.bias_stride))) return MGF_ERR_ALIGNMENT;
     if (g.epilogue == MGF_EPI_SWIGLU) {
       if (g.bias == nullptr || g.d2 == nullptr || (g.n % 16) != 0) return MGF_ERR_INVALID_ARGUMENT;
@@ -1179,13 +1226,20 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     p.n_tiles = n_tiles;
     if (g.total_rows == 0) return MGF_OK;  // nothing to compute, outputs have no rows
     cg = pick_cta_group(false, g.total_rows, g.num_groups, 0);
+    // one stage = 128 bytes of K per row: 64 bf16 or 128 e4m3 elements
+    const CUtensorMapDataType abt = f8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint32_t bke = static_cast<uint32_t>(p.bke);
     const uint64_t dA[2] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.total_rows)};
-    const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * 2};
-    const uint32_t bA[2] = {64, 128};
-    if (!encode_bf16(&tA, g.a, 2, dA, sA, bA)) return MGF_ERR_CUDA;
+    const uint64_t sA[1] = {static_cast<uint64_t>(g.lda) * esz};
+    const uint32_t bA[2] = {bke, 128};
+    if (!encode_bf16(&tA, g.a, 2, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B, abt)) return MGF_ERR_CUDA;
     tD = tA;  // unused by the ragged-M epilogues
-    const uint64_t sB[2] = {static_cast<uint64_t>(g.ldb) * 2, static_cast<uint64_t>(g.ldb_batch) * 2};
-    if (g.b_mn_major) {
+    const uint64_t sB[2] = {static_cast<uint64_t>(g.ldb) * esz, static_cast<uint64_t>(g.ldb_batch) * esz};
+    if (f8) {
+      const uint64_t dB[3] = {static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.num_groups)};
+      const uint32_t bB[3] = {bke, static_cast<uint32_t>(bn / cg), 1};
+      if (!encode_bf16(&tB, g.b, 3, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B, abt)) return MGF_ERR_CUDA;
+    } else if (g.b_mn_major) {
       const uint64_t dB[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.k), static_cast<uint64_t>(g.num_groups)};
       const uint32_t bB[3] = {64, 64, 1};
       if (!encode_bf16(&tB, g.b, 3, dB, sB, bB)) return MGF_ERR_CUDA;
@@ -1273,15 +1327,15 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   }
   if (cg == 2) {
     switch (bn) {
-      case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
-      case 192: return dispatch_epi<192, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
-      default: return dispatch_epi<128, 2>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+      case 256: return dispatch_epi<256, 2>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
+      case 192: return dispatch_epi<192, 2>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
+      default: return dispatch_epi<128, 2>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
     }
   }
   switch (bn) {
-    case 256: return dispatch_epi<256, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
-    case 192: return dispatch_epi<192, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
-    default: return dispatch_epi<128, 1>(g.epilogue, b_mn, tA, tB, tD, p, grid, st);
+    case 256: return dispatch_epi<256, 1>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
+    case 192: return dispatch_epi<192, 1>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
+    default: return dispatch_epi<128, 1>(g.epilogue, b_mn, f8, tA, tB, tD, p, grid, st);
   }
 }
 

@@ -147,6 +147,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]; 8-bit float inputs (kind::f8f6f4, K = 32 per instruction), fp32
+// accumulate, one CTA.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all tcgen05 operations issued so far by this thread completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -254,6 +266,16 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc,
       : "memory");
 }
 
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on the mbarrier at the same offset in every CTA of `cta_mask` once the pair's tcgen05
 // operations issued so far completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
@@ -282,6 +304,18 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_m
   return (1u << 4)                                   // D format: f32
          | (1u << 7)                                 // A format: bf16
          | (1u << 10)                                // B format: bf16
+         | ((a_mn_major ? 1u : 0u) << 15)            // A major
+         | ((b_mn_major ? 1u : 0u) << 16)            // B major
+         | ((static_cast<uint32_t>(N) >> 3) << 17)   // N >> 3
+         | ((static_cast<uint32_t>(M) >> 4) << 24);  // M >> 4
+}
+
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0 in both fields) and
+// fp32 accumulate.
+__host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                                   // D format: f32
+         | (0u << 7)                                 // A format: e4m3
+         | (0u << 10)                                // B format: e4m3
          | ((a_mn_major ? 1u : 0u) << 15)            // A major
          | ((b_mn_major ? 1u : 0u) << 16)            // B major
          | ((static_cast<uint32_t>(N) >> 3) << 17)   // N >> 3

@@ -353,6 +353,97 @@ Tensor mm_downproj_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::opt
   return mm_cuda(mat_a, mat_b, offs, bias, -1);
 }
 
+// ---------------------------------------------------------------- grouped_mm::mm_fp8 / mm_swiglu_fp8
+// Forward-only e4m3 variants of the ragged-M launches (BIAS and SWIGLU epilogues): mat_a [total_M, K]
+// row-major e4m3 with per-row fp32 scales scale_a [total_M]; mat_b [E, K, N] e4m3 with unit stride
+// along K (the transpose of a contiguous [E, N, K]) with per-(expert, column) scales scale_b [E, N].
+// The accumulator is dequantised in fp32 (acc * scale_a[row] * scale_b[e, col]) before the bf16 bias
+// and the epilogue; outputs are bf16 exactly as in mm / mm_swiglu.
+void launch_ragged_m_f8(int epi, const Tensor& a, const Tensor& b, const Tensor& offs, const Tensor& scale_a,
+                        const Tensor& scale_b, const Tensor* bias, const Tensor& d, const Tensor* d2, double alpha,
+                        double limit, bool store_aux, const char* what) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && scale_a.is_cuda() && scale_b.is_cuda(), what,
+              ": inputs must be CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, what,
+              ": mat_a and mat_b must be float8_e4m3fn");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 3, what, ": requires mat_a 2D and mat_b 3D (ragged-M path)");
+  TORCH_CHECK(a.size(1) == b.size(1), "contraction dimension of mat_a and mat_b must match");
+  TORCH_CHECK(a.stride(1) == 1 && a.stride(0) % 16 == 0, what, ": mat_a must be row-major with a 16-byte row pitch");
+  TORCH_CHECK(b.stride(1) == 1 && b.stride(2) % 16 == 0 && b.stride(0) % 16 == 0, what,
+              ": mat_b must have unit stride along K (mat_b[e] = W[e].t() of a contiguous [E, N, K])");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              what, ": data pointers must be 16-byte aligned");
+  check_offs(offs, a);
+  TORCH_CHECK(offs.size(0) == b.size(0), "matrix batch sizes have to match");
+  const int64_t N = b.size(2);
+  TORCH_CHECK(scale_a.scalar_type() == at::kFloat && scale_a.dim() == 1 && scale_a.size(0) == a.size(0) &&
+                  scale_a.is_contiguous(),
+              what, ": scale_a must be a contiguous float32 [total_M]");
+  TORCH_CHECK(scale_b.scalar_type() == at::kFloat && scale_b.dim() == 2 && scale_b.size(0) == b.size(0) &&
+                  scale_b.size(1) == N && scale_b.stride(1) == 1 && scale_b.stride(0) % 4 == 0,
+              what, ": scale_b must be a float32 [E, N] with unit column stride");
+  mgf_gemm_desc g = base_desc();
+  g.epilogue = epi;
+  g.ab_type = MGF_AB_E4M3;
+  g.num_groups = static_cast<int32_t>(offs.numel());
+  g.total_rows = a.size(0);
+  g.k = a.size(1);
+  g.n = N;
+  g.a = a.data_ptr();
+  g.lda = a.stride(0);
+  g.b = b.data_ptr();
+  g.b_mn_major = 0;
+  g.ldb = b.stride(2);
+  g.ldb_batch = b.stride(0);
+  g.offs = offs.data_ptr<int32_t>();
+  g.scale_a = scale_a.data_ptr<float>();
+  g.scale_b = scale_b.data_ptr<float>();
+  g.scale_b_stride = scale_b.stride(0);
+  if (bias != nullptr) {
+    g.bias = bias->data_ptr();
+    g.bias_stride = bias->stride(0);
+  }
+  g.d = d.data_ptr();
+  g.ldd = d.stride(0);
+  if (d2 != nullptr) {
+    g.d2 = d2->data_ptr();
+    g.ldd2 = d2->stride(0);
+  }
+  g.swiglu_alpha = static_cast<float>(alpha);
+  g.swiglu_limit = static_cast<float>(limit);
+  g.store_aux = store_aux ? 1 : 0;
+  g.sm_carveout = sm_carveout_for(a);
+  check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
+}
+
+Tensor mm_fp8_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& scale_a,
+                   const Tensor& scale_b, const std::optional<Tensor>& bias) {
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  const int64_t N = mat_b.size(2);
+  if (bias.has_value()) check_bias(*bias, mat_b.size(0), N);
+  TORCH_CHECK(N % 8 == 0, "grouped_mm_fp8: N must be a multiple of 8");
+  Tensor out = at::empty_strided({mat_a.size(0), N}, {padded(N), 1}, mat_a.options().dtype(at::kBFloat16));
+  launch_ragged_m_f8(MGF_EPI_BIAS, mat_a, mat_b, offs, scale_a, scale_b, bias.has_value() ? &*bias : nullptr, out,
+                     nullptr, 1.702, 7.0, false, "grouped_mm_fp8");
+  return out;
+}
+
+std::tuple<Tensor, Tensor> mm_swiglu_fp8_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                              const Tensor& scale_a, const Tensor& scale_b, const Tensor& bias,
+                                              double alpha, double limit) {
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  const int64_t N = mat_b.size(2);
+  TORCH_CHECK(N % 16 == 0, "grouped_mm_swiglu_fp8: 2*I must be a multiple of 16, got ", N);
+  check_bias(bias, mat_b.size(0), N);
+  const int64_t M = mat_a.size(0);
+  auto opts = mat_a.options().dtype(at::kBFloat16);
+  Tensor swiglu_out = at::empty_strided({M, N / 2}, {padded(N / 2), 1}, opts);
+  Tensor aux_out = at::empty_strided({M, N}, {padded(N), 1}, opts);
+  launch_ragged_m_f8(MGF_EPI_SWIGLU, mat_a, mat_b, offs, scale_a, scale_b, &bias, aux_out, &swiglu_out, alpha, limit,
+                     true, "grouped_mm_swiglu_fp8");
+  return {swiglu_out, aux_out};
+}
+
 // ---------------------------------------------------------------- grouped_mm::mm_wgrad_bias
 // Weight gradient of a ragged-M layer fused with its bias gradient: for every group e,
 // dW[e] = mat_a[:, rows(e)] @ mat_b[rows(e), :] and db[e] = sum over rows(e) of mat_b (fp32
@@ -467,6 +558,10 @@ TORCH_LIBRARY(grouped_mm, m) {
       "mm_swiglu_noaux(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha,"
       " float swiglu_limit) -> Tensor");
   m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
+  m.def("mm_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor? bias) -> Tensor");
+  m.def(
+      "mm_swiglu_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor bias,"
+      " float swiglu_alpha, float swiglu_limit) -> (Tensor, Tensor)");
   m.def("gather_rows(Tensor src, Tensor idx, Tensor? scale) -> Tensor");
   m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
   m.def(
@@ -480,6 +575,8 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_swiglu_noaux", &mm_swiglu_noaux_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
+  m.impl("mm_fp8", &mm_fp8_cuda);
+  m.impl("mm_swiglu_fp8", &mm_swiglu_fp8_cuda);
   m.impl("gather_rows", &gather_rows_cuda);
   m.impl("combine_rows", &combine_rows_cuda);
   m.impl("push_rows", &push_rows_cuda);

@@ -109,7 +109,16 @@ typedef struct mgf_gemm_desc {
   int32_t bias_per_row;  /* BIAS, ragged-M only: 0 = bias[e, col] added to every row (the MoE case);
                             1 = bias[e, row - group start] added to every column of a row (the
                             transposed form of the reference's ragged-N bias, csrc/grouped_mm_common.cuh:107-118) */
+  int32_t ab_type;       /* enum mgf_ab_type: element type of A and B.  MGF_AB_E4M3 (8-bit float,
+                            BIAS and SWIGLU only, B with unit stride along k): the accumulator is
+                            scaled by scale_a[row] * scale_b[e * scale_b_stride + col] before the
+                            bias; lda / ldb / ldb_batch then count bytes (multiples of 16). */
+  const float* scale_a;  /* E4M3: device fp32 [total_rows] */
+  const float* scale_b;  /* E4M3: device fp32 [E, n] */
+  int64_t scale_b_stride;
 } mgf_gemm_desc;
+
+enum mgf_ab_type { MGF_AB_BF16 = 0, MGF_AB_E4M3 = 1 };
 
 /* Launch one grouped GEMM on `stream` (a cudaStream_t; NULL = legacy default stream).
  * Replaces: csrc/binding.cu:13-148 (the three pybind entry points) + the dispatch in

@@ -150,3 +150,34 @@ def test_fake_shape_ragged_n():
     offs = _meta(3, dtype=torch.int32)
     out = m.grouped_mm(_meta(3, 72, 64), _meta(64, 208), offs)
     assert out.shape == (72, 208)
+
+
+def test_fp8_ops_registered_and_shapes():
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    _pkg()
+    E, K, N, M = 4, 256, 128, 300
+    a = torch.empty(M, K, dtype=torch.float8_e4m3fn, device="meta")
+    b = torch.empty(E, N, K, dtype=torch.float8_e4m3fn, device="meta").transpose(1, 2)
+    offs = _meta(E, dtype=torch.int32)
+    sa, sb = _meta(M, dtype=torch.float32), _meta(E, N, dtype=torch.float32)
+    assert fp8.grouped_mm_fp8(a, b, offs, sa, sb).shape == (M, N)
+    s, aux = fp8.grouped_mm_swiglu_fp8(a, b, offs, sa, sb, _meta(E, N))
+    assert s.shape == (M, N // 2) and aux.shape == (M, N)
+
+
+def test_fp8_quantizers_round_trip():
+    """Row-wise e4m3 quantisation keeps every element within e4m3's relative step of its value."""
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(37, 72, generator=g)
+    q, s = fp8.quantize_rows(x)
+    assert q.dtype == torch.float8_e4m3fn and q.stride(0) % 16 == 0 and s.shape == (37,)
+    err = (fp8.dequantize_rows(q, s) - x).abs()
+    assert (err <= x.abs() * 2 ** -3 + s[:, None] * 2 ** -6).all()
+    w = torch.randn(3, 72, 40, generator=g)
+    qw, sw = fp8.quantize_weights(w)
+    assert qw.shape == (3, 72, 40) and qw.stride(1) == 1 and sw.shape == (3, 40)
+    errw = (fp8.dequantize_weights(qw, sw) - w).abs()
+    assert (errw <= w.abs() * 2 ** -3 + sw[:, None, :] * 2 ** -6).all()

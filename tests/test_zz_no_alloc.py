@@ -32,7 +32,9 @@ class MgfGemmDesc(ctypes.Structure):
                 ("ldd", ctypes.c_int64), ("ldd_batch", ctypes.c_int64), ("d2", ctypes.c_void_p),
                 ("ldd2", ctypes.c_int64), ("aux", ctypes.c_void_p), ("ld_aux", ctypes.c_int64),
                 ("swiglu_alpha", ctypes.c_float), ("swiglu_limit", ctypes.c_float), ("store_aux", ctypes.c_int32),
-                ("sm_carveout", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("bias_per_row", ctypes.c_int32)]
+                ("sm_carveout", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("bias_per_row", ctypes.c_int32),
+                ("ab_type", ctypes.c_int32), ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
+                ("scale_b_stride", ctypes.c_int64)]
 
 
 MGF_EPI_WGRAD = 3
