@@ -3,7 +3,7 @@
 Run in the build container (the reference is mounted read-only at REF_ROOT; nothing at test time
 reads it):
 
-    python tests/golden/make_golden.py [REF_ROOT]
+    python tests/golden/make_golden.py REF_ROOT
 
 It loads Butterfingrz/CuTe-MoE-Train's ``cutlass_op/bf16_grouped_mm/__init__.py`` and
 ``custom_op.py`` unmodified under the module name ``ref_bf16_grouped_mm`` and injects a CPU
@@ -167,7 +167,9 @@ def run_reference(ref, x, w_up, b_up, w_down, b_down, offs, gout):
 
 
 def main():
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py REF_ROOT  (the reference project's root)")
+    ref_root = Path(sys.argv[1])
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = load_reference(ref_root)
     fixtures = {"cases": {}, "generator": "tests/golden/make_golden.py", "alpha": 1.702, "limit": 7.0}
