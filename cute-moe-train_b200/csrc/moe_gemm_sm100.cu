@@ -1274,7 +1274,9 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
       const uint32_t boxA3[3] = {64, 64, static_cast<uint32_t>(BM / 64)};
       const uint32_t boxB3[3] = {64, 64, static_cast<uint32_t>((bn / cg + 63) / 64)};
       p.a_chunked = (g.m % 64) == 0 ? 1 : 0;
-      p.b_chunked = (g.n % 64) == 0 ? 1 : 0;
+      // (each CTA's first column, n_blk * BN + crank * BN / CG, must start a chunk: not so for
+      // CTA pairs with BN = 192, whose halves are 96 columns wide)
+      p.b_chunked = ((g.n % 64) == 0 && ((bn / cg) % 64) == 0) ? 1 : 0;
       if (p.a_chunked) {
         const uint64_t dA[3] = {64, static_cast<uint64_t>(g.total_rows), static_cast<uint64_t>(g.m / 64)};
         const uint64_t sA[2] = {static_cast<uint64_t>(g.lda) * 2, 128};

@@ -88,8 +88,14 @@ def test_config1_vs_oracle():
         (6, 384, 96, [0, 0, 513, 0, 64, 0]),
     ],
 )
-def test_chain_shapes(E, H, I, counts):
+@pytest.mark.parametrize("cg", ["auto", "1", "2"])
+def test_chain_shapes(E, H, I, counts, cg, monkeypatch):
+    """Every launch of the chain with the default CTA policy, forced single CTAs and forced pairs
+    (ragged-K pairs included)."""
     from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    if cg != "auto":
+        monkeypatch.setenv("MGF_CTA_GROUP", cg)
 
     x, w_up, b_up, w_down, b_down, offs, gout = small_case(E, H, I, counts, seed=E * 1000 + H)
     got = _run_chain(x, w_up, b_up, w_down, b_down, offs, gout)
