@@ -440,6 +440,15 @@ def main():
     # end-to-end through the public API with host buffers
     if world == 1 and not args.no_e2e:
         line["e2e"] = e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops_local, fwd_only)
+    elif world > 1 and not args.no_e2e:
+        e2e = e2e_run_ep(ffn, x, expert_idx, args, barrier)
+        t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms_per_step"] = float(t[0])
+        e2e["value"] = flops_all / (e2e["ms_per_step"] * 1e-3) / 1e12
+        e2e["unit"] = UNIT
+        if rank == 0:
+            line["e2e"] = e2e
 
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         tf, rows, t = cpu_sample_tflops(H, I, target_s=12.0, max_rows=65536)
@@ -549,6 +558,54 @@ def e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops, fwd_o
             "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + offs_host.numel() * 4,
             "d2h_bytes_per_step": 4,
             "h2d": "pinned host -> device on a copy stream, one step ahead (double-buffered prefetch)"}
+
+
+def e2e_run_ep(ffn, x, expert_idx, args, barrier):
+    """Expert-parallel step through EPMoEFFN with each rank's token rows and routing copied from pinned
+    host memory every step (on a copy stream, one step ahead, double-buffered, the last copy inside
+    the timed window) and the loss read back.  Returns this rank's ms per step; the caller takes the
+    max over ranks."""
+    import torch
+
+    x_host = x.detach().to("cpu").pin_memory()
+    idx_host = expert_idx.to("cpu").pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    x_dev = [torch.empty_like(x.detach()) for _ in range(2)]
+    idx_dev = [torch.empty_like(expert_idx) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    copy_stream = torch.cuda.Stream()
+    state = {"i": 0}
+
+    def issue_copy(slot):
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[slot])
+            x_dev[slot].copy_(x_host, non_blocking=True)
+            idx_dev[slot].copy_(idx_host, non_blocking=True)
+            ready[slot].record(copy_stream)
+
+    issue_copy(0)
+
+    def step():
+        slot = state["i"] & 1
+        state["i"] += 1
+        issue_copy(slot ^ 1)
+        torch.cuda.current_stream().wait_event(ready[slot])
+        ffn.zero_grad()
+        xl = x_dev[slot].detach().requires_grad_(True)
+        loss = ffn(xl, idx_dev[slot]).sum(dtype=torch.float32)
+        loss.backward()
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        free[slot].record()
+
+    def tail():
+        torch.cuda.current_stream().wait_stream(copy_stream)
+
+    ms = time_steps(step, args.steps, args.warmup, barrier=barrier, tail=tail)
+    return {"ms_per_step": ms,
+            "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + idx_host.numel() * idx_host.element_size(),
+            "d2h_bytes_per_step": 4,
+            "h2d": "per rank: pinned host -> device on a copy stream, one step ahead (double-buffered prefetch)"}
 
 
 if __name__ == "__main__":
