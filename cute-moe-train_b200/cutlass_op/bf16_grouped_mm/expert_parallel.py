@@ -17,7 +17,11 @@ forward
 backward mirrors it: the all-to-alls are differentiable (their gradient is the reverse exchange) and
 the expert weight gradients stay local -- pure EP needs no gradient all-reduce.
 
-No kernel reads a peer's memory; all exchanged rows land in this GPU's memory through NCCL first.
+Two transports carry the rows.  ``ep_moe_ffn`` (above; CPU/gloo and ``transport="nccl"``) uses NCCL
+all-to-alls with host-side split sizes.  ``ep_moe_ffn_peer`` (CUDA, the default of ``EPMoEFFN``) has
+each source rank write its rows straight into the owners' receive buffers through CUDA IPC mappings
+(``grouped_mm::push_rows``: plain peer stores, no TMA, no multicast), with the whole plan computed on
+the device and one-element all-reduces as stream-ordered barriers.  No kernel reads a peer's memory.
 ``expert_fn`` can replace the fused FFN (e.g. with a CPU reference for gloo tests of the routing).
 """
 
