@@ -20,7 +20,12 @@
 //   warp 1      TMEM allocator + UMMA issuer; for ragged-K it also patches the K tail of the
 //               last stage (zero rows past the group end) and writes the bias-gradient "ones" row
 //   warps 2..9  epilogue (two warpgroups, each half of the tile's columns): TMEM -> registers ->
-//               fused math -> predicated global stores
+//               fused math -> predicated 16/32-byte global stores (ragged-M) or per-warp 32 x 32
+//               TMA tile stores from shared memory (ragged-K)
+//
+// CTA pairs (CG = 2, cluster of two, cta_group::2 MMAs on 256-row tiles) for ragged-M launches whose
+// groups are large; single CTAs (128-row tiles) otherwise and for ragged-K.  F8 = true is the e4m3
+// variant of the ragged-M BIAS / SWIGLU launches (kind::f8f6f4, row-wise scales in the epilogue).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
