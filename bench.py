@@ -240,7 +240,9 @@ def reference_arm(args, rank, world):
         return
     import torch
 
-    H = I = 2880
+    # the same workload description, metric and unit as this arm's GPU line; the CPU times a bounded
+    # sample of it (the rate is per routed row, so the sample size does not change the metric)
+    _, desc, E_total, _, tokens, topk, H, I, _, _ = build_workload(args, rank, world, None)
     torch.set_num_threads(os.cpu_count() or 1)
     # size one step so the whole run stays within a few minutes
     per_step_target = max(1.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
@@ -266,7 +268,9 @@ def reference_arm(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)", "data": "synthetic",
-        "config": {"workload": "cfg3 shape, bounded CPU sample", "H": H, "I": I, "rows_per_step": rows},
+        "config": {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
+                   "cpu_sample": f"each step: the oracle chain on {rows} routed rows of this shape (bounded sample)",
+                   "rows_per_step": rows},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
