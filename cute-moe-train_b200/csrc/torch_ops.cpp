@@ -307,6 +307,73 @@ std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat
   return swiglu_launch(mat_a, mat_b, offs, bias, alpha, limit, true);
 }
 
+// ---------------------------------------------------------------- into-output forms (the reference binding)
+// csrc/binding.cu:36-63 `_grouped_mm_swiglu_cuda(mat_a, mat_b, offs, bias, aux_out, swiglu_out, alpha,
+// limit, store_aux)`: the caller allocates swiglu_out [M, I] (and aux_out [M, 2I] when store_aux);
+// the launch writes them in place.
+void swiglu_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
+                      const std::optional<Tensor>& aux_out, const Tensor& swiglu_out, double alpha, double limit,
+                      bool store_aux) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm_swiglu: inputs must be CUDA tensors");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 3, "grouped_mm_swiglu requires mat_a 2D and mat_b 3D (ragged-M path)");
+  TORCH_CHECK(mat_a.scalar_type() == at::kBFloat16 && mat_b.scalar_type() == at::kBFloat16,
+              "grouped_mm_swiglu requires BFloat16 inputs");
+  TORCH_CHECK(bias.scalar_type() == at::kBFloat16, "bias must be BFloat16");
+  TORCH_CHECK(offs.scalar_type() == at::kInt, "offs must be int32");
+  if (store_aux) {
+    TORCH_CHECK(aux_out.has_value(), "grouped_mm_swiglu(store_aux=True) requires aux_out tensor");
+    TORCH_CHECK(aux_out->scalar_type() == at::kBFloat16, "aux_out must be BFloat16");
+  }
+  TORCH_CHECK(mat_a.size(1) == mat_b.size(1), "contraction dimension of mat_a and mat_b must match");
+  TORCH_CHECK(!check_strides_transposed(mat_a, "mat_a"), "grouped_mm_swiglu requires a row-major mat_a");
+  check_offs(offs, mat_a);
+  TORCH_CHECK(offs.size(0) == mat_b.size(0), "matrix batch sizes have to match");
+  const int64_t M = mat_a.size(0), N = mat_b.size(2);
+  TORCH_CHECK(N % 16 == 0, "grouped_mm_swiglu: 2*I must be a multiple of 16, got ", N);
+  check_bias(bias, mat_b.size(0), N);
+  TORCH_CHECK(swiglu_out.scalar_type() == at::kBFloat16 && swiglu_out.dim() == 2 && swiglu_out.size(0) == M &&
+                  swiglu_out.size(1) == N / 2 && swiglu_out.stride(1) == 1,
+              "swiglu_out must be a row-major bf16 [M, I]");
+  if (store_aux)
+    TORCH_CHECK(aux_out->dim() == 2 && aux_out->size(0) == M && aux_out->size(1) == N && aux_out->stride(1) == 1,
+                "aux_out must be a row-major bf16 [M, 2*I]");
+  launch_ragged_m(MGF_EPI_SWIGLU, mat_a, mat_b, offs, &bias, store_aux ? *aux_out : swiglu_out, &swiglu_out, nullptr,
+                  alpha, limit, store_aux, "grouped_mm_swiglu");
+}
+
+// csrc/binding.cu:68-118 `_grouped_mm_swiglu_bwd_cuda(grad_output, down_w_t, offs, aux_packed,
+// grad_gate_up_packed, alpha, limit)`: aux and the result are the fp32 [M, I] views of bf16 (gate, up)
+// pairs; the result is written in place.
+void swiglu_bwd_into_cuda(const Tensor& grad_output, const Tensor& down_w_t, const Tensor& offs,
+                          const Tensor& aux_packed, const Tensor& grad_packed, double alpha, double limit) {
+  TORCH_CHECK(grad_output.dim() == 2, "grad_output must be 2D [M, H]");
+  TORCH_CHECK(down_w_t.dim() == 3, "down_w_t must be 3D [E, H, I]");
+  TORCH_CHECK(aux_packed.dim() == 2, "aux_packed must be 2D [M, I]");
+  TORCH_CHECK(grad_packed.dim() == 2, "grad_gate_up_packed must be 2D [M, I]");
+  TORCH_CHECK(offs.dim() == 1, "offs must be 1D [E]");
+  TORCH_CHECK(grad_output.scalar_type() == at::kBFloat16 && down_w_t.scalar_type() == at::kBFloat16,
+              "_grouped_mm_swiglu_bwd_cuda requires bf16 grad_output and down_w_t");
+  TORCH_CHECK(aux_packed.scalar_type() == at::kFloat, "aux_packed must be float32");
+  TORCH_CHECK(grad_packed.scalar_type() == at::kFloat, "grad_gate_up_packed must be float32");
+  TORCH_CHECK(offs.scalar_type() == at::kInt, "offs must be int32");
+  TORCH_CHECK(grad_output.size(0) == aux_packed.size(0) && aux_packed.sizes() == grad_packed.sizes(),
+              "Expected [M, I] packed tensors with matching shape");
+  TORCH_CHECK(down_w_t.size(0) == offs.size(0), "down_w_t.shape[0] must match offs.size(0)");
+  TORCH_CHECK(grad_output.size(1) == down_w_t.size(1), "grad_output.shape[1] must match down_w_t.shape[1] (H)");
+  TORCH_CHECK(down_w_t.size(2) == aux_packed.size(1), "down_w_t.shape[2] must match aux_packed.shape[1] (I)");
+  TORCH_CHECK(grad_output.device() == down_w_t.device() && down_w_t.device() == offs.device() &&
+                  offs.device() == aux_packed.device() && aux_packed.device() == grad_packed.device(),
+              "All tensors must be on the same device");
+  TORCH_CHECK(aux_packed.stride(1) == 1 && grad_packed.stride(1) == 1, "packed tensors must be row-major");
+  const c10::cuda::CUDAGuard guard(grad_output.device());
+  if (grad_output.numel() == 0) return;
+  const Tensor aux = aux_packed.view(at::kBFloat16);  // [M, 2I]
+  const Tensor grad = grad_packed.view(at::kBFloat16);
+  launch_ragged_m(MGF_EPI_SWIGLU_BWD, grad_output.contiguous(), down_w_t, offs, nullptr, grad, nullptr, &aux, alpha,
+                  limit, false, "grouped_mm_swiglu_bwd");
+}
+
 // ---------------------------------------------------------------- grouped_mm::mm_swiglu_noaux
 Tensor mm_swiglu_noaux_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
                             double alpha, double limit) {
@@ -558,6 +625,12 @@ TORCH_LIBRARY(grouped_mm, m) {
       "mm_swiglu_noaux(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, float swiglu_alpha,"
       " float swiglu_limit) -> Tensor");
   m.def("mm_wgrad_bias(Tensor mat_a, Tensor mat_b, Tensor offs) -> (Tensor, Tensor)");
+  m.def(
+      "swiglu_into(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, Tensor(a!)? aux_out, Tensor(b!) swiglu_out,"
+      " float swiglu_alpha, float swiglu_limit, bool store_aux) -> ()");
+  m.def(
+      "swiglu_bwd_into(Tensor grad_output, Tensor down_w_t, Tensor offs, Tensor aux_packed,"
+      " Tensor(a!) grad_gate_up_packed, float swiglu_alpha, float swiglu_limit) -> ()");
   m.def("mm_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor? bias) -> Tensor");
   m.def(
       "mm_swiglu_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor bias,"
@@ -573,6 +646,8 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm", &mm_cuda);
   m.impl("mm_swiglu", &mm_swiglu_cuda);
   m.impl("mm_swiglu_noaux", &mm_swiglu_noaux_cuda);
+  m.impl("swiglu_into", &swiglu_into_cuda);
+  m.impl("swiglu_bwd_into", &swiglu_bwd_into_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
   m.impl("mm_fp8", &mm_fp8_cuda);

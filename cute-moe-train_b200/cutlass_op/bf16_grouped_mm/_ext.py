@@ -94,3 +94,36 @@ def check_device_status(device: int | None = None) -> None:
         if st & DEV_BAD_OFFS:
             what.append("offs was not non-decreasing within [0, total rows]")
         raise RuntimeError("grouped_mm device status: " + "; ".join(what))
+
+
+# ------------------------------------------------------------------------ the reference binding's API
+# Butterfingrz/CuTe-MoE-Train exposes three functions from its compiled `_ext` module
+# (cutlass_op/bf16_grouped_mm/csrc/binding.cu:121-145); its custom_op.py calls them, and so may code
+# that imports `_ext` directly.  Same names, arguments, defaults and in-place outputs here.
+
+def _grouped_mm_cuda(mat_a: torch.Tensor, mat_b: torch.Tensor, offs: torch.Tensor | None = None,
+                     bias: torch.Tensor | None = None, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Grouped GEMM (+ per-group bias); returns a new output (csrc/binding.cu:13-34)."""
+    from .custom_op import dtype_to_int
+
+    return torch.ops.grouped_mm.mm(mat_a, mat_b, offs, bias, dtype_to_int(out_dtype))
+
+
+def _grouped_mm_swiglu_cuda(mat_a: torch.Tensor, mat_b: torch.Tensor, offs: torch.Tensor, bias: torch.Tensor,
+                            aux_out: torch.Tensor | None = None, swiglu_out: torch.Tensor | None = None,
+                            swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, store_aux: bool = True) -> None:
+    """Fused GEMM + bias + SwiGLU into the caller's `swiglu_out` (and `aux_out` when store_aux)
+    (csrc/binding.cu:36-63)."""
+    if swiglu_out is None:
+        raise TypeError("_grouped_mm_swiglu_cuda: swiglu_out is required")
+    torch.ops.grouped_mm.swiglu_into(mat_a, mat_b, offs, bias, aux_out, swiglu_out, swiglu_alpha, swiglu_limit,
+                                     store_aux)
+
+
+def _grouped_mm_swiglu_bwd_cuda(grad_output: torch.Tensor, down_w_t: torch.Tensor, offs: torch.Tensor,
+                                aux_packed: torch.Tensor, grad_gate_up_packed: torch.Tensor,
+                                swiglu_alpha: float, swiglu_limit: float) -> None:
+    """Fused down-proj dgrad + SwiGLU backward into `grad_gate_up_packed` (fp32 [M, I] views of bf16
+    pairs, csrc/binding.cu:68-118)."""
+    torch.ops.grouped_mm.swiglu_bwd_into(grad_output, down_w_t, offs, aux_packed, grad_gate_up_packed,
+                                         swiglu_alpha, swiglu_limit)

@@ -444,6 +444,19 @@ class GroupedFFN(torch.autograd.Function):
         return g_x, g_wu, g_bu, g_wd, g_bd, None, None, None, None
 
 
+# ============================================================================ into-output forms
+
+
+@torch.library.register_fake("grouped_mm::swiglu_into")
+def _swiglu_into_fake(mat_a, mat_b, offs, bias, aux_out, swiglu_out, swiglu_alpha, swiglu_limit, store_aux):
+    return None
+
+
+@torch.library.register_fake("grouped_mm::swiglu_bwd_into")
+def _swiglu_bwd_into_fake(grad_output, down_w_t, offs, aux_packed, grad_gate_up_packed, swiglu_alpha, swiglu_limit):
+    return None
+
+
 # ============================================================================ EP row movement
 
 

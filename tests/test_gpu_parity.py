@@ -182,3 +182,33 @@ def test_ffn_recompute_equals_stored_aux(counts):
     ref = O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, gout)
     got = dict(zip(names, res[False]))
     _compare_chain(got, ref, offs, keys=names)
+
+
+def test_reference_binding_functions_match_the_operators():
+    """`_ext._grouped_mm_swiglu_cuda` / `_grouped_mm_swiglu_bwd_cuda` write into the caller's buffers
+    exactly what the operators return (store_aux on and off; the packed fp32 views of the reference)."""
+    m = _lib()
+    from cutlass_op.bf16_grouped_mm import _ext
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(3, 128, 64, [70, 0, 131], seed=21)
+    x, w_up, b_up, w_down, offs, gout = (t.cuda() for t in (x, w_up, b_up, w_down, offs, gout))
+    s_ref, aux_ref = m.grouped_mm_swiglu(x, w_up, offs, b_up)
+    M, I = x.shape[0], w_up.shape[2] // 2
+    s_out = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    aux_out = torch.empty(M, 2 * I, dtype=torch.bfloat16, device="cuda")
+    _ext._grouped_mm_swiglu_cuda(x, w_up, offs, b_up, aux_out, s_out, 1.702, 7.0, True)
+    rows = int(offs[-1])
+    assert torch.equal(s_out[:rows], s_ref[:rows]) and torch.equal(aux_out[:rows], aux_ref[:rows])
+    s_only = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    _ext._grouped_mm_swiglu_cuda(x, w_up, offs, b_up, None, s_only, 1.702, 7.0, False)
+    assert torch.equal(s_only[:rows], s_ref[:rows])
+    g_ref = torch.ops.grouped_mm.mm_swiglu_bwd(gout, w_down.cuda().transpose(-2, -1), offs, aux_ref, 1.702, 7.0)
+    g_packed = torch.empty(M, I, dtype=torch.float32, device="cuda")
+    _ext._grouped_mm_swiglu_bwd_cuda(gout, w_down.cuda().transpose(-2, -1), offs, aux_ref.view(torch.float32),
+                                     g_packed, 1.702, 7.0)
+    torch.cuda.synchronize()
+    m.check_device_status()
+    assert torch.equal(g_packed.view(torch.bfloat16)[:rows], g_ref[:rows])
+    out = _ext._grouped_mm_cuda(s_ref, w_down.cuda(), offs, None, None)
+    assert torch.equal(out[:rows], m.grouped_mm(s_ref, w_down.cuda(), offs)[:rows])

@@ -181,3 +181,20 @@ def test_fp8_quantizers_round_trip():
     assert qw.shape == (3, 72, 40) and qw.stride(1) == 1 and sw.shape == (3, 40)
     errw = (fp8.dequantize_weights(qw, sw) - w).abs()
     assert (errw <= w.abs() * 2 ** -3 + sw[:, None, :] * 2 ** -6).all()
+
+
+def test_reference_binding_functions():
+    """The reference's compiled `_ext` functions exist with its argument names and defaults
+    (csrc/binding.cu:121-145)."""
+    from cutlass_op.bf16_grouped_mm import _ext
+
+    s = inspect.signature(_ext._grouped_mm_cuda)
+    assert list(s.parameters) == ["mat_a", "mat_b", "offs", "bias", "out_dtype"]
+    assert all(s.parameters[k].default is None for k in ("offs", "bias", "out_dtype"))
+    s = inspect.signature(_ext._grouped_mm_swiglu_cuda)
+    assert list(s.parameters) == ["mat_a", "mat_b", "offs", "bias", "aux_out", "swiglu_out", "swiglu_alpha",
+                                  "swiglu_limit", "store_aux"]
+    assert s.parameters["aux_out"].default is None and s.parameters["store_aux"].default is True
+    s = inspect.signature(_ext._grouped_mm_swiglu_bwd_cuda)
+    assert list(s.parameters) == ["grad_output", "down_w_t", "offs", "aux_packed", "grad_gate_up_packed",
+                                  "swiglu_alpha", "swiglu_limit"]
