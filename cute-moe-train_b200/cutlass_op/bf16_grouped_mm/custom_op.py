@@ -475,3 +475,40 @@ grouped_mm_forward = torch.ops.grouped_mm.mm
 grouped_mm_swiglu_forward = torch.ops.grouped_mm.mm_swiglu
 grouped_mm_swiglu_bwd_forward = torch.ops.grouped_mm.mm_swiglu_bwd
 grouped_mm_downproj_forward = torch.ops.grouped_mm.mm_downproj
+
+# ... and its autograd pieces and helpers (custom_op.py:12-131, 190-330, 353-397, 467-693), for code
+# that imports them: this module's equivalents under the reference's names.
+grouped_mm_setup_context = _mm_setup_context
+grouped_mm_backward = _mm_backward
+grouped_mm_swiglu_setup_context = _swiglu_setup_context
+grouped_mm_swiglu_backward = _swiglu_backward
+grouped_mm_downproj_setup_context = _downproj_setup_context
+grouped_mm_downproj_backward = _downproj_backward
+_segment_sum_rows = segment_sum_rows
+_segment_sum_cols = segment_sum_cols  # groups columns exactly like the forward's bias (see segment_sum_cols)
+_infer_grouped_mm_out_shape = _out_shape
+_empty_grouped_mm_output = _empty_out
+
+
+def _infer_grouped_mm_out_strides(out_shape, out_dtype, *, a_is_2d: bool, b_is_2d: bool) -> tuple[int, ...]:
+    """Row-major strides with the last dimension padded to 16 bytes; 2D output for ragged-M / ragged-N."""
+    last = _padded(out_shape[-1], out_dtype)
+    if a_is_2d != b_is_2d:
+        return (last, 1)
+    return (out_shape[1] * last, last, 1)
+
+
+def _empty_swiglu_output(mat_a, mat_b, offs=None) -> torch.Tensor:
+    """swiglu_out [total_M, I] bf16 with the 16-byte padded row stride."""
+    half = mat_b.size(-1) // 2
+    return torch.empty_strided((mat_a.size(0), half), (_padded(half, torch.bfloat16), 1), dtype=torch.bfloat16,
+                               device=mat_a.device)
+
+
+def _as_packed_fp32(tensor_bf16: torch.Tensor, *, tensor_name: str) -> torch.Tensor:
+    """The fp32 [..., I] view of interleaved bf16 (gate, up) pairs [..., 2I]."""
+    if tensor_bf16.dtype != torch.bfloat16:
+        raise RuntimeError(f"{tensor_name} must be bfloat16, got {tensor_bf16.dtype}")
+    if tensor_bf16.size(-1) % 2 or tensor_bf16.stride(-1) != 1 or tensor_bf16.stride(-2) % 2:
+        raise RuntimeError(f"{tensor_name} must be row-major with an even last dimension and row stride")
+    return tensor_bf16.view(torch.float32)

@@ -198,3 +198,20 @@ def test_reference_binding_functions():
     s = inspect.signature(_ext._grouped_mm_swiglu_bwd_cuda)
     assert list(s.parameters) == ["grad_output", "down_w_t", "offs", "aux_packed", "grad_gate_up_packed",
                                   "swiglu_alpha", "swiglu_limit"]
+
+
+def test_reference_module_names_present():
+    """Every module-level function / name the reference's custom_op.py defines exists here."""
+    import cutlass_op.bf16_grouped_mm.custom_op as c
+
+    names = ["grouped_mm_forward", "grouped_mm_swiglu_forward", "grouped_mm_swiglu_bwd_forward",
+             "grouped_mm_downproj_forward", "grouped_mm_setup_context", "grouped_mm_backward",
+             "grouped_mm_swiglu_setup_context", "grouped_mm_swiglu_backward", "grouped_mm_downproj_setup_context",
+             "grouped_mm_downproj_backward", "_segment_sum_rows", "_segment_sum_cols", "_infer_grouped_mm_out_shape",
+             "_infer_grouped_mm_out_strides", "_empty_grouped_mm_output", "_empty_swiglu_output", "_as_packed_fp32",
+             "_dtype_from_int", "_has_effective_grad"]
+    assert [n for n in names if not hasattr(c, n)] == []
+    assert c._infer_grouped_mm_out_strides((10, 36), torch.bfloat16, a_is_2d=True, b_is_2d=False) == (40, 1)
+    assert c._infer_grouped_mm_out_strides((3, 10, 36), torch.bfloat16, a_is_2d=True, b_is_2d=True) == (400, 40, 1)
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    assert c._as_packed_fp32(x, tensor_name="x").shape == (4, 4)
