@@ -215,3 +215,17 @@ def test_reference_module_names_present():
     assert c._infer_grouped_mm_out_strides((3, 10, 36), torch.bfloat16, a_is_2d=True, b_is_2d=True) == (400, 40, 1)
     x = torch.zeros(4, 8, dtype=torch.bfloat16)
     assert c._as_packed_fp32(x, tensor_name="x").shape == (4, 4)
+
+
+def test_segment_sum_rows_matches_a_loop():
+    """Ragged-M bias gradient (custom_op.py:79-101): fp32 row sums per group; rows past offs[-1] and
+    empty groups contribute nothing."""
+    from cutlass_op.bf16_grouped_mm.custom_op import segment_sum_rows
+
+    g = torch.randn(11, 6, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    offs = torch.tensor([4, 4, 9], dtype=torch.int32)  # group 1 empty, rows 9-10 in no group
+    got = segment_sum_rows(g, offs)
+    ref = torch.zeros(3, 6)
+    ref[0] = g[0:4].float().sum(0)
+    ref[2] = g[4:9].float().sum(0)
+    assert got.dtype == torch.bfloat16 and torch.equal(got, ref.to(torch.bfloat16))
