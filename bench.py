@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the MoE FFN grouped-GEMM path on B200.
 
-Metric (BASELINE.json): MoE FFN fwd+bwd ms and BF16 TFLOP/s per GPU (24K tokens per rank), % of
+Metric: MoE FFN fwd+bwd ms and BF16 TFLOP/s per GPU (24K tokens per rank), % of
 tensor peak.  One step = grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward() over the
 routed rows of 24576 tokens (top-4): useful FLOPs 18*M*H*I (M = routed rows on this GPU).
 
@@ -66,6 +66,8 @@ def parse_args():
                          "(the extra GEMM's FLOPs are not counted in the metric)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="N=1: skip the secondary measurements (cfg2 forward, cfg5 at 4096 tokens, cfg4 at N=1)")
     ap.add_argument("--tokens", type=int, default=0,
                     help="tokens per GPU (default 24576; cfg5 default 4096; smaller for profiling cases)")
     ap.add_argument("--experts", type=int, default=0, help="override the number of experts (profiling cases)")
@@ -170,11 +172,41 @@ def build_workload(args, rank, world, device):
             desc = f"cfg2: forward-only grouped_mm_swiglu, E={E_total} H=I=2880, {tokens} tokens top-4 Zipf(1.1)"
         return wl, desc, E_total, zero, tokens, topk, H, I, 1.1, wl == "cfg2"
     E_total = args.experts or 128
-    desc = (f"cfg4: GPT-OSS-120B experts E=128 H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
+    desc = (f"cfg4: GPT-OSS-120B experts E={E_total} H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
             f"expert parallel E/{world} per GPU, dispatch/combine by "
             + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all")
             + (", dispatch gradient pushed under the up-proj wgrad" if args.ep_overlap else ""))
     return wl, desc, E_total, 0, tokens, topk, H, I, 1.1, False
+
+
+def line_config(args, world):
+    """The `config` object of the JSON line: identical for this arm and the reference arm."""
+    wl, desc, E_total, _, tokens, topk, H, I, _, fwd_only = build_workload(args, 0, world, None)
+    return {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (x 566 MB + weights >= 1.6 GB per GPU), no flush",
+            "step": (("grouped_mm_swiglu_fp8 forward only (config 2 shapes, row-wise e4m3 inputs "
+                      "quantised before the timed region)" if args.fp8 else
+                      "grouped_mm_swiglu forward only (config 2)") if fwd_only else
+                     "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
+                     "(the metric is the MoE FFN fwd+bwd)"
+                     + ("; store_aux=False: aux recomputed in backward, 18*M*H*I FLOPs counted"
+                        if args.recompute_aux else ""))}
+
+
+def load_workloads_module():
+    """workloads.py by file path: the seeded generators without importing the product package
+    (whose __init__ loads the native libraries)."""
+    import importlib.util
+
+    path = PKG / "cutlass_op" / "bf16_grouped_mm" / "workloads.py"
+    if "mgf_bench_workloads" in sys.modules:
+        return sys.modules["mgf_bench_workloads"]
+    spec = importlib.util.spec_from_file_location("mgf_bench_workloads", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["mgf_bench_workloads"] = mod  # dataclasses look their module up here
+    spec.loader.exec_module(mod)
+    return mod
 
 
 # ------------------------------------------------------------------------------------- runs
@@ -203,79 +235,361 @@ def time_steps(step_fn, steps, warmup, barrier=None, sync=None, tail=None):
     return a.elapsed_time(b) / steps
 
 
-def cpu_sample_tflops(H, I, target_s, max_rows=16384):
-    """Time the oracle (CPU restatement of the reference's chain) fwd+bwd on S rows of the shape,
-    repeated until at least target_s seconds of CPU work were timed; returns (TFLOP/s, S, seconds)."""
+REF_LAYER = REPO / "baseline" / "_ref" / "group_gemm"
+
+
+class CpuReference:
+    """The reference's CPU path for this workload, timed on the host cores.
+
+    Preferred: the reference's own, unmodified Python layer (its __init__.py + custom_op.py staged
+    under baseline/_ref by baseline/stage_reference.py: autograd routing, fused-only contract,
+    _segment_sum_rows) over oracle/ref_ext_cpu.py, a CPU restatement of its three CUDA kernels
+    (kind "reference").  Without the staged layer: the oracle port oracle/moe_ffn.kernel_chain
+    (kind "port").  Neither loads any of this repository's native libraries."""
+
+    def __init__(self):
+        import torch
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cores = torch.get_num_threads()
+        self.ref = None
+        if (REF_LAYER / "custom_op.py").is_file():
+            from oracle.ref_ext_cpu import load_reference_layer
+
+            self.ref = load_reference_layer(REF_LAYER, modname="ref_group_gemm")
+            self.kind = "reference"
+            self.what = ("the reference's unmodified Python layer (baseline/_ref/group_gemm: __init__.py + "
+                         "custom_op.py) over a CPU restatement of its three CUDA kernels (oracle/ref_ext_cpu.py), "
+                         "torch fp32 GEMMs on bf16 inputs")
+        else:
+            self.kind = "port"
+            self.what = "the oracle port (oracle/moe_ffn.kernel_chain, fp32 torch CPU restatement of the chain)"
+
+    def step(self, case):
+        x, w_up, b_up, w_down, b_down, offs = case
+        if self.ref is None:
+            from oracle import moe_ffn as O
+
+            g = __import__("torch").ones(x.shape[0], w_down.shape[-1], dtype=x.dtype)
+            O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, g)
+            return
+        leaves = [t.detach().requires_grad_(True) for t in (x, w_up, b_up, w_down, b_down)]
+        xl, wu, bu, wd, bd = leaves
+        s_, aux = self.ref.grouped_mm_swiglu(xl, wu, offs=offs, bias=bu, swiglu_alpha=ALPHA, swiglu_limit=LIMIT)
+        out = self.ref.grouped_mm_downproj(s_, wd, offs=offs, bias=bd, aux_biased_acc=aux, swiglu_alpha=ALPHA,
+                                           swiglu_limit=LIMIT)
+        out.sum().backward()
+
+
+def cpu_counts(args, world):
+    """Tokens per local expert of rank 0's workload (the same routing the GPU arm uses)."""
     import torch
 
-    from cutlass_op.bf16_grouped_mm.workloads import small_case
-    from oracle import moe_ffn as O
+    wlm = load_workloads_module()
+    wl, _, E_total, zero, tokens, topk, H, I, zipf_s, fwd_only = build_workload(args, 0, world, None)
+    if world == 1:
+        if wl == "cfg5":
+            return wlm.config5_counts(tokens, E_total, topk, seed=0), H, I, fwd_only
+        return wlm.zipf_routing(tokens, E_total, topk, zipf_s, seed=0, zero_experts=zero), H, I, fwd_only
+    # expert parallel: rank 0 owns E/N experts and receives ~tokens*topk rows from all ranks
+    e_local = E_total // world
+    rows = tokens * topk
+    c = torch.full((e_local,), rows // e_local, dtype=torch.int64)
+    c[: rows % e_local] += 1
+    return c, H, I, fwd_only
 
-    torch.set_num_threads(os.cpu_count() or 1)
 
-    def case(rows):
-        return small_case(2, H, I, [rows // 2, rows - rows // 2], seed=123)
+def cpu_case(counts, H, I, seed=123):
+    import math
 
-    def run(c):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    E, M = counts.numel(), int(counts.sum())
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    w_up = (torch.randn(E, H, 2 * I, generator=g) / math.sqrt(H)).to(torch.bfloat16)
+    b_up = (torch.randn(E, 2 * I, generator=g) * 0.02).to(torch.bfloat16)
+    w_down = (torch.randn(E, I, H, generator=g) / math.sqrt(I)).to(torch.bfloat16)
+    b_down = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    offs = torch.cumsum(counts, 0).to(torch.int32)
+    return x, w_up, b_up, w_down, b_down, offs
+
+
+def cpu_sample_tflops(args, world, target_s=12.0):
+    """cpu_baseline of this arm's line: the CPU reference on a bounded sample of the workload -- the
+    first experts of its routing, whole, up to about a quarter of the rows -- repeated until about
+    target_s seconds of CPU work were timed."""
+    cref = CpuReference()
+    counts, H, I, _ = cpu_counts(args, world)
+    keep, rows = 0, 0
+    for c in counts.tolist():
+        if rows >= max(1, int(counts.sum()) // 4):
+            break
+        keep += 1
+        rows += c
+    case = cpu_case(counts[:keep], H, I)
+    t0 = time.perf_counter()
+    cref.step(case)
+    reps, total = 1, time.perf_counter() - t0
+    while total < target_s and reps < 20:
         t0 = time.perf_counter()
-        O.kernel_chain(*c)
-        return time.perf_counter() - t0
-
-    rows = 1024
-    t = run(case(rows))
-    rows = int(max(256, min(max_rows, rows * (target_s / 4) / max(t, 1e-3))))
-    rows -= rows % 8
-    c = case(rows)
-    total, reps = 0.0, 0
-    while total < target_s and reps < 50:
-        total += run(c)
+        cref.step(case)
+        total += time.perf_counter() - t0
         reps += 1
-    flops = 18.0 * rows * H * I * reps
-    return flops / total / 1e12, rows, total
+    value = 18.0 * rows * H * I * reps / total / 1e12
+    sample = (f"{cref.what}: fwd+bwd of the first {keep} of {counts.numel()} experts of this workload's routing "
+              f"({rows} routed rows, H={H}, I={I}), {reps} repetitions, {total:.1f} s of CPU work")
+    return {"value": value, "unit": UNIT, "cores": cref.cores, "kind": cref.kind, "sample": sample}
 
 
 def reference_arm(args, rank, world):
-    """--impl reference: the oracle port of the reference's CPU path, timed on the host cores."""
+    """--impl reference: the reference's CPU path (CpuReference) on this arm's workload and config,
+    timed on the host cores.  Each step runs the whole workload of rank 0 when K + W such steps fit
+    in REF_BUDGET_S seconds; otherwise each step is a bounded sample of it -- the first experts of
+    its routing, whole -- sized from a calibration step so that the run fits (stated in the line)."""
     if rank != 0:
         return
-    import torch
-
-    # the same workload description, metric and unit as this arm's GPU line; the CPU times a bounded
-    # sample of it (the rate is per routed row, so the sample size does not change the metric)
-    _, desc, E_total, _, tokens, topk, H, I, _, _ = build_workload(args, rank, world, None)
-    torch.set_num_threads(os.cpu_count() or 1)
-    # size one step so the whole run stays within a few minutes
-    per_step_target = max(1.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
-    tf, rows, t = cpu_sample_tflops(H, I, per_step_target)
-    from cutlass_op.bf16_grouped_mm.workloads import small_case
-    from oracle import moe_ffn as O
-
-    counts = [rows // 2, rows - rows // 2]
-    case = small_case(2, H, I, counts, seed=123)
+    cref = CpuReference()
+    counts, H, I, fwd_only = cpu_counts(args, world)
+    if fwd_only:
+        raise SystemExit("--impl reference times the fwd+bwd workloads (cfg3/cfg4/cfg5)")
+    total_rows = int(counts.sum())
+    # calibration on about an eighth of the experts
+    n_cal = max(1, counts.numel() // 8)
+    cal = cpu_case(counts[:n_cal], H, I)
+    cref.step(cal)
+    t0 = time.perf_counter()
+    cref.step(cal)
+    t_cal = time.perf_counter() - t0
+    rows_cal = max(1, int(counts[:n_cal].sum()))
+    per_row = t_cal / rows_cal
+    allowed = REF_BUDGET_S / max(1, args.steps + args.warmup)
+    keep, rows = 0, 0
+    for c in counts.tolist():
+        if keep and (rows + c) * per_row > allowed:
+            break
+        keep += 1
+        rows += c
+    del cal
+    case = cpu_case(counts[:keep], H, I)
     for _ in range(args.warmup):
-        O.kernel_chain(*case)
+        cref.step(case)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.kernel_chain(*case)
+        cref.step(case)
         times.append(time.perf_counter() - t0)
     step_s = sum(times) / len(times)
-    flops = 18.0 * rows * H * I
-    value = flops / step_s / 1e12
-    sample = (f"oracle port (fp32 torch CPU restatement of the reference chain) fwd+bwd on {rows} routed rows "
-              f"over 2 experts of the H=I=2880 shape per step")
+    value = 18.0 * rows * H * I / step_s / 1e12
+    whole = keep == counts.numel()
+    sample = (f"{cref.what}: fwd+bwd with out.sum(); every step " +
+              (f"the whole workload of rank 0 ({counts.numel()} experts, {rows} routed rows" if whole else
+               f"a bounded sample of rank 0's workload: its first {keep} of {counts.numel()} experts, whole "
+               f"({rows} of {total_rows} routed rows; the full step would take ~{per_row * total_rows:.0f} s here")
+              + f", H={H}, I={I}); malloc keeps freed memory (no page-fault churn)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)", "data": "synthetic",
-        "config": {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
-                   "cpu_sample": f"each step: the oracle chain on {rows} routed rows of this shape (bounded sample)",
-                   "rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": sample},
+        "config": line_config(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cref.cores, "kind": cref.kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "rows_per_step": rows, "routed_rows_rank0": total_rows, "whole_workload_per_step": whole,
     }
     print(json.dumps(line), flush=True)
+
+
+# glibc malloc settings for the CPU legs: keep freed memory in the process instead of returning each
+# large block to the kernel and faulting it in again (the CPU path allocates GB-sized temporaries
+# every step; without this, page faults roughly double its time).
+MALLOC_ENV = {"MALLOC_MMAP_THRESHOLD_": str(16 << 30), "MALLOC_TRIM_THRESHOLD_": str(64 << 30),
+              "MALLOC_TOP_PAD_": str(1 << 30)}
+REF_BUDGET_S = 200.0
+
+
+def _reexec_with_malloc_env():
+    if all(os.environ.get(k) == v for k, v in MALLOC_ENV.items()):
+        return
+    env = dict(os.environ, **MALLOC_ENV)
+    os.execve(sys.executable, [sys.executable] + sys.argv, env)
+
+
+def ep_parity_check(args, world, rank, device):
+    """Before the timed region at N > 1: a small expert-parallel fwd+bwd (512 tokens per rank, 8
+    experts per rank, H=256, I=128, top-4, Zipf routing, router weights, random output gradient)
+    through the same transport as the bench; rank 0 gathers every rank's inputs, weights and
+    results and checks outputs, token, router-weight and all expert weight/bias gradients against
+    the single-process oracle (oracle/ep_ffn.py, used here only as the checker)."""
+    import torch
+    import torch.distributed as dist
+
+    from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+    T, E, H, I, K = 512, 8 * world, 256, 128, 4
+    ffn = EPMoEFFN(E, H, I, device=device, seed=77, transport=args.transport, overlap=args.ep_overlap)
+    g = torch.Generator().manual_seed(500 + rank)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, K, generator=g)
+    gout = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    idx = route_tokens(T, E, K, "zipf", seed=600 + rank)
+    xd, wd = x.to(device).requires_grad_(True), w.to(device).requires_grad_(True)
+    out = ffn(xd, idx.to(device), wd)
+    out.backward(gout.to(device))
+    torch.cuda.synchronize()
+    mine = {"x": x, "idx": idx, "w": w, "g": gout,
+            "got": [t.detach().cpu() for t in (out, xd.grad, wd.grad, ffn.w_up.grad, ffn.b_up.grad,
+                                              ffn.w_down.grad, ffn.b_down.grad)],
+            "weights": [p.detach().cpu() for p in (ffn.w_up, ffn.b_up, ffn.w_down, ffn.b_down)]}
+    allr = [None] * world
+    dist.all_gather_object(allr, mine)
+    del ffn
+    if rank != 0:
+        return None
+    from oracle import moe_ffn as O
+    from oracle.ep_ffn import ep_reference
+
+    wts = [torch.cat([r["weights"][i] for r in allr], 0) for i in range(4)]
+    want = ep_reference([r["x"] for r in allr], [r["idx"] for r in allr], [r["w"] for r in allr],
+                        [r["g"] for r in allr], *wts)
+    e_local = E // world
+    worst_rel, worst_cos, ok, n = 0.0, 1.0, True, 0
+    for rk, r in enumerate(allr):
+        sl = slice(rk * e_local, (rk + 1) * e_local)
+        refs = [want["out"][rk], want["dx"][rk], want["dw_router"][rk], want["dw_up"][sl], want["db_up"][sl],
+                want["dw_down"][sl], want["db_down"][sl]]
+        for got, ref in zip(r["got"], refs):
+            c = O.check("ep", got.float(), ref.float())
+            worst_rel, worst_cos, ok, n = max(worst_rel, c["rel"]), min(worst_cos, c["cos"]), ok and c["ok"], n + 1
+    return {"ok": ok, "max_rel": worst_rel, "min_cos": worst_cos, "tensors_checked": n,
+            "case": f"{world} ranks x {T} tokens, E={E} H={H} I={I} top-{K} Zipf, router weights, random grad, "
+                    f"transport {args.transport}" + (" + overlap" if args.ep_overlap else "")}
+
+
+def roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=False):
+    """Live per-kernel roofline of the step: achieved TFLOP/s of the dominant operator (FLOPs per
+    launch / its CUDA-event average) against the measured burst bf16 peak, the sustained one beside."""
+    names = [k for k in ops if k in OP_FLOP_UNITS]
+    if not names:
+        return None
+    name = max(names, key=lambda k: ops[k]["total_ms"])
+    fl = OP_FLOP_UNITS[name] * float(local_rows) * H * I
+    ach = fl / (ops[name]["avg_ms"] * 1e-3) / 1e12
+    peak, peak_name = peaks["bf16_tflops"], f"{peak_src} bf16_tflops (burst)"
+    if fp8:  # no measured e4m3 peak on this pool: the nominal dense figure
+        peak, peak_name = 4500.0, "nominal e4m3 dense 4.5 PFLOP/s (no measured fp8 peak)"
+    traffic = load_traffic()
+    tr = None
+    if traffic and traffic.get("op") == name:
+        tr = traffic.get("bytes_per_launch")
+    return {"bound": "tensor", "kernel": name, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+            "frac": ach / peak, "peak_source": peak_name,
+            "frac_of_sustained": ach / peaks["bf16_tflops_sustained"],
+            "traffic": tr, "traffic_source": (traffic or {}).get("how") if tr else None,
+            "algorithmic_flop_per_launch": fl,
+            "ops": {k: {"avg_ms": round(v["avg_ms"], 4), "launches": v["launches"],
+                        "tflops": OP_FLOP_UNITS.get(k, 0) * float(local_rows) * H * I / (v["avg_ms"] * 1e-3) / 1e12}
+                    for k, v in ops.items()}}
+
+
+def single_gpu_setup(args, wl, E, zero, tokens, topk, H, I, zipf_s, device):
+    """Seeded routing, inputs and weights of a 1-GPU workload on `device`."""
+    import torch
+
+    from cutlass_op.bf16_grouped_mm.workloads import (MoEShape, config5_counts, make_weights_device,
+                                                      offs_from_counts, zipf_routing)
+
+    if wl == "cfg5":
+        counts = config5_counts(tokens, E, topk, seed=0)
+    else:
+        counts = zipf_routing(tokens, E, topk, zipf_s, seed=0, zero_experts=zero)
+    M = int(counts.sum())
+    offs = offs_from_counts(counts).to(device)
+    gx = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(M, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
+    w_up, b_up, w_down, b_down = [t.requires_grad_(True) for t in
+                                  make_weights_device(MoEShape(E, H, I), seed=2, device=device)]
+    return counts, M, offs, x, w_up, b_up, w_down, b_down
+
+
+def ffn_step_fn(mgf, params, offs, fwd_only=False, recompute=False):
+    import torch
+
+    x, w_up, b_up, w_down, b_down = params
+
+    def step():
+        for p in params:
+            p.grad = None
+        if fwd_only:
+            with torch.no_grad():
+                mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
+            return
+        if recompute:
+            out = mgf.grouped_mm_ffn(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT, store_aux=False)
+        else:
+            s_, aux = mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
+            out = mgf.grouped_mm_downproj(s_, w_down, offs, b_down, aux, ALPHA, LIMIT)
+        out.sum().backward()
+    return step
+
+
+def extra_workloads(args, mgf, device, peaks, peak_src):
+    """Secondary 1-GPU measurements carried in the same JSON line (not the headline): config 2
+    (forward only), config 5 at 4096 tokens (the HBM-bound fine-grained corner) and config 4's
+    one-GPU point (E=128 through the expert-parallel module on one rank: the N=1 anchor of the
+    expert-parallel scaling curve)."""
+    import torch
+
+    from cutlass_op.bf16_grouped_mm.optimer import OpTimer
+
+    steps, warm = max(3, min(args.steps, 20)), max(3, min(args.warmup, 5))
+    out = {}
+    for name, wl, E, zero, tokens, topk, H, I, zs, fwd in (
+            ("cfg2_fwd", "cfg2", 32, 0, 24576, 4, 2880, 2880, 1.1, True),
+            ("cfg5_t4096", "cfg5", 256, 0, 4096, 8, 7168, 2048, 1.3, False)):
+        try:
+            counts, M, offs, x, w_up, b_up, w_down, b_down = single_gpu_setup(
+                args, wl, E, zero, tokens, topk, H, I, zs, device)
+            step = ffn_step_fn(mgf, [x, w_up, b_up, w_down, b_down], offs, fwd_only=fwd)
+            for _ in range(warm):
+                step()
+            timer = OpTimer().install()
+            ms = time_steps(step, steps, 0)
+            timer.uninstall()
+            fl = (4.0 if fwd else 18.0) * M * H * I
+            roof = roofline_entry(timer.summary(), M, H, I, peaks, peak_src)
+            out[name] = {"ms_per_step": ms, "tflops": fl / (ms * 1e-3) / 1e12, "routed_rows": M, "steps": steps,
+                         "E": E, "H": H, "I": I, "tokens": tokens, "topk": topk,
+                         "ops": roof["ops"] if roof else None}
+            del x, w_up, b_up, w_down, b_down, step
+        except Exception as e:  # report, do not fail the bench
+            out[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        torch.cuda.empty_cache()
+    try:
+        from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+        E, H, I, T, K = 128, 2880, 2880, 24576, 4
+        res = {}
+        for routing in ("uniform", "zipf"):
+            ffn = EPMoEFFN(E, H, I, group=None, device=device, seed=2)
+            x = torch.randn(T, H, generator=torch.Generator(device=device).manual_seed(1), device=device)
+            x = x.to(torch.bfloat16).requires_grad_(True)
+            idx = route_tokens(T, E, K, routing, seed=100, device=device)
+
+            def step():
+                x.grad = None
+                ffn.zero_grad()
+                ffn(x, idx).sum().backward()
+            for _ in range(warm):
+                step()
+            ms = time_steps(step, steps, 0)
+            res[routing] = {"ms_per_step": ms, "tflops": 18.0 * T * K * H * I / (ms * 1e-3) / 1e12}
+            del ffn, x, step
+            torch.cuda.empty_cache()
+        out["cfg4_n1"] = dict(res, what="cfg4 at N=1: E=128 H=I=2880, 24576 tokens top-4 through EPMoEFFN on "
+                                        "one rank (local gather/permute/combine, no exchange)")
+    except Exception as e:
+        out["cfg4_n1"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    return out
 
 
 def main():
@@ -284,8 +598,13 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if rank != 0:
+            return
+        _reexec_with_malloc_env()
         reference_arm(args, rank, world)
         return
+    if world == 1 and not args.no_cpu_baseline:
+        _reexec_with_malloc_env()
 
     import torch
     import torch.distributed as dist
@@ -298,25 +617,15 @@ def main():
 
     import cutlass_op.bf16_grouped_mm as mgf
     from cutlass_op.bf16_grouped_mm.optimer import OpTimer
-    from cutlass_op.bf16_grouped_mm.workloads import MoEShape, make_weights_device, offs_from_counts, zipf_routing
 
     wl, desc, E_total, zero, tokens, topk, H, I, zipf_s, fwd_only = build_workload(args, rank, world, device)
     peaks, peak_src = load_peaks()
+    ep_parity = None
 
     if world == 1:
         E = E_total
-        if wl == "cfg5":
-            from cutlass_op.bf16_grouped_mm.workloads import config5_counts
-
-            counts = config5_counts(tokens, E, topk, seed=0)
-        else:
-            counts = zipf_routing(tokens, E, topk, zipf_s, seed=0, zero_experts=zero)
-        M = int(counts.sum())
-        offs = offs_from_counts(counts).to(device)
-        gx = torch.Generator(device=device).manual_seed(1)
-        x = torch.randn(M, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
-        w_up, b_up, w_down, b_down = [t.requires_grad_(True) for t in
-                                      make_weights_device(MoEShape(E, H, I), seed=2, device=device)]
+        counts, M, offs, x, w_up, b_up, w_down, b_down = single_gpu_setup(
+            args, wl, E, zero, tokens, topk, H, I, zipf_s, device)
         params = [x, w_up, b_up, w_down, b_down]
         if args.fp8:
             if not fwd_only:
@@ -327,26 +636,17 @@ def main():
                 qx, sx = fp8_mod.quantize_rows(x.detach())
                 qw, sw = fp8_mod.quantize_weights(w_up.detach())
 
-        def step():
-            for p in params:
-                p.grad = None
-            if fwd_only:
+            def step():
                 with torch.no_grad():
-                    if args.fp8:
-                        fp8_mod.grouped_mm_swiglu_fp8(qx, qw, offs, sx, sw, b_up, ALPHA, LIMIT)
-                    else:
-                        mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
-                return
-            if args.recompute_aux:
-                out = mgf.grouped_mm_ffn(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT, store_aux=False)
-            else:
-                s, aux = mgf.grouped_mm_swiglu(x, w_up, offs, b_up, ALPHA, LIMIT)
-                out = mgf.grouped_mm_downproj(s, w_down, offs, b_down, aux, ALPHA, LIMIT)
-            out.sum().backward()
+                    fp8_mod.grouped_mm_swiglu_fp8(qx, qw, offs, sx, sw, b_up, ALPHA, LIMIT)
+        else:
+            step = ffn_step_fn(mgf, params, offs, fwd_only=fwd_only, recompute=args.recompute_aux)
         local_rows = M
     else:
         from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
+        ep_parity = ep_parity_check(args, world, rank, device)
+        torch.cuda.empty_cache()
         ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport,
                        overlap=args.ep_overlap)
         gx = torch.Generator(device=device).manual_seed(1 + rank)
@@ -391,58 +691,35 @@ def main():
         ms_max, flops_all = ms, flops_local
     value = flops_all / (ms_max * 1e-3) / 1e12
     per_gpu = value / world
-
-    # dominant kernel roofline (tensor-bound GEMMs)
-    roof = None
-    ours_launches = sum(v["launches"] for k, v in ops.items() if k in OP_FLOP_UNITS)
-    if ops:
-        name = max((k for k in ops if k in OP_FLOP_UNITS), key=lambda k: ops[k]["total_ms"])
-        fl = OP_FLOP_UNITS[name] * float(local_rows) * H * I
-        ach = fl / (ops[name]["avg_ms"] * 1e-3) / 1e12
-        peak = peaks["bf16_tflops_sustained"]
-        peak_name = f"{peak_src} bf16_tflops_sustained"
-        if args.fp8:  # no measured e4m3 peak on this pool: the nominal dense figure
-            peak, peak_name = 4500.0, "nominal e4m3 dense 4.5 PFLOP/s (no measured fp8 peak)"
-        traffic = load_traffic()
-        roof = {"bound": "tensor", "kernel": name, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                "frac": ach / peak, "peak_source": peak_name,
-                "traffic": (traffic or {}).get("bytes_per_launch") if (traffic or {}).get("op") == name else None,
-                "algorithmic_flop_per_launch": fl,
-                "ops": {k: {"avg_ms": round(v["avg_ms"], 4), "launches": v["launches"],
-                            "tflops": OP_FLOP_UNITS.get(k, 0) * float(local_rows) * H * I / (v["avg_ms"] * 1e-3) / 1e12}
-                        for k, v in ops.items()}}
+    ours_launches = sum(v["launches"] for k, v in ops.items() if k in OP_FLOP_UNITS or k.startswith("ep_"))
+    roof = roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=args.fp8) if ops else None
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out" if args.fp8 else "bf16",
         "data": "synthetic (seeded, shapes of the configured workload)",
-        "config": {"workload": desc, "E": E_total, "H": H, "I": I, "tokens_per_gpu": tokens, "topk": topk,
-                   "routed_rows_gpu0": local_rows, "parallelism": f"ep{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (x 566 MB + weights >= 1.6 GB per GPU), no flush",
-                   "step": (("grouped_mm_swiglu_fp8 forward only (config 2 shapes, row-wise e4m3 inputs "
-                             "quantised before the timed region)" if args.fp8 else
-                             "grouped_mm_swiglu forward only (config 2)") if fwd_only else
-                            "grouped_mm_swiglu -> grouped_mm_downproj -> out.sum().backward(); no optimizer "
-                            "(the metric is the MoE FFN fwd+bwd)"
-                            + ("; store_aux=False: aux recomputed in backward, 18*M*H*I FLOPs counted"
-                               if args.recompute_aux else ""))},
+        "config": line_config(args, world),
+        "routed_rows_gpu0": local_rows,
         "tflops_per_gpu": per_gpu,
-        "pct_of_peak": 100.0 * per_gpu / peaks["bf16_tflops_sustained"],
-        "peak_tflops": peaks["bf16_tflops_sustained"], "peak_source": f"{peak_src} bf16_tflops_sustained",
+        "pct_of_peak": 100.0 * per_gpu / peaks["bf16_tflops"],
+        "peak_tflops": peaks["bf16_tflops"], "peak_source": f"{peak_src} bf16_tflops (burst)",
+        "pct_of_sustained_peak": 100.0 * per_gpu / peaks["bf16_tflops_sustained"],
         "gpu_launches": int(ours_launches),
         "roofline": roof,
         "clocks": clocks,
     }
+    if ep_parity is not None:
+        line["ep_parity"] = ep_parity
 
     # torch._grouped_mm + eager bias/SwiGLU on the same inputs (single GPU only)
-    if world == 1 and not args.no_compare:
+    if world == 1 and not args.no_compare and not args.fp8:
         line["torch_grouped_mm"] = compare_torch(step_inputs=(x, w_up, b_up, w_down, b_down, offs, counts),
                                                  steps=args.steps, warmup=args.warmup, flops=flops_local,
                                                  fwd_only=fwd_only)
 
     # end-to-end through the public API with host buffers
-    if world == 1 and not args.no_e2e:
+    if world == 1 and not args.no_e2e and not args.fp8:
         line["e2e"] = e2e_run(mgf, x, w_up, b_up, w_down, b_down, offs, counts, args, flops_local, fwd_only)
     elif world > 1 and not args.no_e2e:
         e2e = e2e_run_ep(ffn, x, expert_idx, args, barrier)
@@ -454,12 +731,14 @@ def main():
         if rank == 0:
             line["e2e"] = e2e
 
+    if world == 1 and not args.no_extra and wl == "cfg3" and not args.tokens and not args.experts:
+        del step
+        params = x = w_up = b_up = w_down = b_down = None
+        torch.cuda.empty_cache()
+        line["extra"] = extra_workloads(args, mgf, device, peaks, peak_src)
+
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        tf, rows, t = cpu_sample_tflops(H, I, target_s=12.0, max_rows=65536)
-        import torch as _t
-        line["cpu_baseline"] = {"value": tf, "unit": UNIT, "cores": _t.get_num_threads(), "kind": "port",
-                                "sample": f"oracle fwd+bwd on {rows} routed rows over 2 experts of the H=I=2880 "
-                                          f"shape, repeated for {t:.1f} s of CPU work, fp32 torch on the host"}
+        line["cpu_baseline"] = cpu_sample_tflops(args, world)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -467,38 +746,61 @@ def main():
 
 
 def compare_torch(step_inputs, steps, warmup, flops, fwd_only=False):
+    """torch._grouped_mm + eager bias / clamped SwiGLU / autograd on the same inputs and GPU.
+
+    The per-expert biases are added in place, one row block per expert (no [M, N] gathered bias
+    tensor).  Besides the whole step it times the same graph without the bias and SwiGLU (the two
+    torch._grouped_mm GEMMs and their autograd alone), so the line shows how the step splits into
+    grouped-GEMM time and eager-op time."""
     import torch
 
     x, w_up, b_up, w_down, b_down, offs, counts = step_inputs
     try:
-        row_e = torch.repeat_interleave(torch.arange(len(counts), device=x.device), counts.to(x.device))
+        bounds = torch.cumsum(counts.cpu(), 0).tolist()
+        starts = [0] + bounds[:-1]
         xs = x.detach().clone().requires_grad_(True)
         wu, bu, wd, bd = [t.detach().clone().requires_grad_(True) for t in (w_up, b_up, w_down, b_down)]
         params = [xs, wu, bu, wd, bd]
         ones = torch.ones(x.shape[0], w_down.shape[-1], dtype=x.dtype, device=x.device)
 
-        def step():
-            for p in params:
-                p.grad = None
-            if fwd_only:
-                with torch.no_grad():
-                    h = torch._grouped_mm(xs, wu, offs=offs) + bu[row_e]
-                    g = h[:, 0::2].clamp(max=LIMIT)
-                    u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
-                    g * torch.sigmoid(ALPHA * g) * (u + 1.0)
-                return
-            h = torch._grouped_mm(xs, wu, offs=offs) + bu[row_e]
-            g = h[:, 0::2].clamp(max=LIMIT)
-            u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
-            s = g * torch.sigmoid(ALPHA * g) * (u + 1.0)
-            out = torch._grouped_mm(s, wd, offs=offs) + bd[row_e]
-            # d(out.sum())/d(out) as a materialised tensor: torch._grouped_mm's backward rejects the
-            # zero-stride expanded gradient that out.sum().backward() produces.
-            out.backward(ones)
+        def add_bias(h, b):
+            # in place on each expert's row block (torch._grouped_mm's backward does not need its output)
+            for e, (s0, s1) in enumerate(zip(starts, bounds)):
+                if s1 > s0:
+                    h[s0:s1] += b[e]
+            return h
 
-        ms = time_steps(step, steps, warmup)
+        def make(eager: bool):
+            def step():
+                for p in params:
+                    p.grad = None
+                ctx = torch.no_grad() if fwd_only else torch.enable_grad()
+                with ctx:
+                    h = torch._grouped_mm(xs, wu, offs=offs)
+                    if eager:
+                        h = add_bias(h, bu)
+                        g = h[:, 0::2].clamp(max=LIMIT)
+                        u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
+                        s_ = g * torch.sigmoid(ALPHA * g) * (u + 1.0)
+                    else:
+                        s_ = h[:, 0::2].contiguous()
+                    if fwd_only:
+                        return
+                    out = torch._grouped_mm(s_, wd, offs=offs)
+                    if eager:
+                        out = add_bias(out, bd)
+                    # d(out.sum())/d(out) as a materialised tensor: torch._grouped_mm's backward rejects the
+                    # zero-stride expanded gradient that out.sum().backward() produces.
+                    out.backward(ones)
+            return step
+
+        ms = time_steps(make(True), steps, warmup)
+        ms_gemm = time_steps(make(False), max(3, steps // 2), warmup)
         return {"ms_per_step": ms, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT,
-                "what": "torch._grouped_mm + eager bias / clamped SwiGLU / autograd, same inputs, same GPU"}
+                "grouped_mm_only_ms": ms_gemm, "eager_ops_ms": ms - ms_gemm,
+                "what": "torch._grouped_mm + eager per-expert bias / clamped SwiGLU / autograd, same inputs, same "
+                        "GPU; grouped_mm_only_ms = the same graph without bias and SwiGLU (the two grouped GEMMs "
+                        "and their autograd), eager_ops_ms = the difference"}
     except Exception as e:  # report, do not fail the bench
         return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 

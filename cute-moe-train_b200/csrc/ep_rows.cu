@@ -30,14 +30,18 @@ __device__ __forceinline__ uint32_t pack(float a, float b) {
 }
 
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) gather_rows_kernel(
-    const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ idx,
+    const __nv_bfloat16* __restrict__ src, int64_t ld_src, int64_t n_src, const int64_t* __restrict__ idx,
     const float* __restrict__ scale, int64_t n_rows, int64_t row_vec, __nv_bfloat16* __restrict__ dst,
-    int64_t ld_dst) {
+    int64_t ld_dst, unsigned int* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t i = warp0; i < n_rows; i += nwarps) {
     const int64_t s = __ldg(idx + i);
+    if (s < 0 || s >= n_src) {  // a wrong plan: report it, leave the output row as it was
+      if (lane == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+      continue;
+    }
     const uint4* sp = reinterpret_cast<const uint4*>(src + s * ld_src);
     uint4* dp = reinterpret_cast<uint4*>(dst + i * ld_dst);
     if (scale == nullptr) {
@@ -54,13 +58,22 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) gather_rows_kernel(
 }
 
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) combine_rows_kernel(
-    const __nv_bfloat16* __restrict__ rows, int64_t ld_rows, const int64_t* __restrict__ pos,
+    const __nv_bfloat16* __restrict__ rows, int64_t ld_rows, int64_t n_rows, const int64_t* __restrict__ pos,
     const float* __restrict__ w, int64_t n_out, int k, int64_t row_vec, __nv_bfloat16* __restrict__ out,
-    int64_t ld_out) {
+    int64_t ld_out, unsigned int* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t t = warp0; t < n_out; t += nwarps) {
+    bool bad = false;
+    for (int j = lane; j < k; j += 32) {
+      const int64_t r = __ldg(pos + t * k + j);
+      bad |= (r < 0 || r >= n_rows);
+    }
+    if (__any_sync(0xffffffffu, bad)) {  // a wrong plan: report it, leave the output row as it was
+      if (lane == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+      continue;
+    }
     uint4* op = reinterpret_cast<uint4*>(out + t * ld_out);
     for (int64_t v = lane; v < row_vec; v += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -86,7 +99,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
     const float* __restrict__ scale, int64_t n_max, const int32_t* __restrict__ n_dev,
     const int64_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
     const unsigned long long* __restrict__ peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
-    int64_t row_vec) {
+    int64_t row_vec, int64_t n_src, unsigned int* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -99,7 +112,11 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
     const int64_t s = src_idx != nullptr ? __ldg(src_idx + i) : i;
     const int64_t r = __ldg(dst_rank + i);
     const int64_t row = __ldg(dst_row + i);
-    if (r < 0 || r >= world || row < 0 || row >= dst_rows) continue;  // never store outside a peer buffer
+    if (r < 0 || r >= world || row < 0 || row >= dst_rows || s < 0 || s >= n_src) {
+      // never store outside a peer buffer nor read outside src; report the skipped row
+      if (lane == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+      continue;
+    }
     __nv_bfloat16* dbase = reinterpret_cast<__nv_bfloat16*>(peer_bases[r]);
     const uint4* sp = reinterpret_cast<const uint4*>(src + s * ld_src);
     uint4* dp = reinterpret_cast<uint4*>(dbase + row * ld_dst);
@@ -130,48 +147,60 @@ int grid_for(int64_t rows) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+// The device status word lives in the GEMM translation unit (moe_gemm_sm100.cu); its device
+// address for the current device comes from there.
+unsigned int* status_word_address();
+
 }  // namespace mgf
 
-extern "C" int mgf_gather_rows(const void* src, int64_t ld_src, const int64_t* idx, const float* scale,
-                               int64_t n_rows, int64_t row_elems, void* dst, int64_t ld_dst, void* stream) {
+extern "C" int mgf_gather_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* idx,
+                               const float* scale, int64_t n_rows, int64_t row_elems, void* dst, int64_t ld_dst,
+                               void* stream) {
   using namespace mgf;
-  if (n_rows < 0 || row_elems < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_rows < 0 || row_elems < 0 || n_src < 0) return MGF_ERR_INVALID_ARGUMENT;
   if (n_rows == 0 || row_elems == 0) return MGF_OK;
   if (src == nullptr || idx == nullptr || dst == nullptr) return MGF_ERR_INVALID_ARGUMENT;
   if (row_elems % 8 || ld_src % 8 || ld_dst % 8 || !aligned16(src) || !aligned16(dst)) return MGF_ERR_ALIGNMENT;
+  unsigned int* status = status_word_address();
+  if (status == nullptr) return MGF_ERR_CUDA;
   gather_rows_kernel<<<grid_for(n_rows), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(src), ld_src, idx, scale, n_rows, row_elems / 8,
-      static_cast<__nv_bfloat16*>(dst), ld_dst);
+      static_cast<const __nv_bfloat16*>(src), ld_src, n_src, idx, scale, n_rows, row_elems / 8,
+      static_cast<__nv_bfloat16*>(dst), ld_dst, status);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 
-extern "C" int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t* pos, const float* weights,
-                                int64_t n_out, int32_t k, int64_t row_elems, void* out, int64_t ld_out,
-                                void* stream) {
+extern "C" int mgf_combine_rows(const void* rows, int64_t ld_rows, int64_t n_rows, const int64_t* pos,
+                                const float* weights, int64_t n_out, int32_t k, int64_t row_elems, void* out,
+                                int64_t ld_out, void* stream) {
   using namespace mgf;
-  if (n_out < 0 || row_elems < 0 || k < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_out < 0 || row_elems < 0 || k < 0 || n_rows < 0) return MGF_ERR_INVALID_ARGUMENT;
   if (n_out == 0 || row_elems == 0) return MGF_OK;
   if (out == nullptr || (k > 0 && (rows == nullptr || pos == nullptr))) return MGF_ERR_INVALID_ARGUMENT;
   if (row_elems % 8 || ld_rows % 8 || ld_out % 8 || !aligned16(rows) || !aligned16(out)) return MGF_ERR_ALIGNMENT;
+  unsigned int* status = status_word_address();
+  if (status == nullptr) return MGF_ERR_CUDA;
   combine_rows_kernel<<<grid_for(n_out), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(rows), ld_rows, pos, weights, n_out, k, row_elems / 8,
-      static_cast<__nv_bfloat16*>(out), ld_out);
+      static_cast<const __nv_bfloat16*>(rows), ld_rows, n_rows, pos, weights, n_out, k, row_elems / 8,
+      static_cast<__nv_bfloat16*>(out), ld_out, status);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 
-extern "C" int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src_idx, const float* scale,
-                             int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
+extern "C" int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* src_idx,
+                             const float* scale, int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
                              const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
                              int64_t row_elems, void* stream) {
   using namespace mgf;
-  if (n_max < 0 || row_elems < 0) return MGF_ERR_INVALID_ARGUMENT;
+  if (n_max < 0 || row_elems < 0 || n_src < 0) return MGF_ERR_INVALID_ARGUMENT;
   if (n_max == 0 || row_elems == 0) return MGF_OK;
   if (src == nullptr || dst_rank == nullptr || dst_row == nullptr || peer_bases == nullptr)
     return MGF_ERR_INVALID_ARGUMENT;
   if (row_elems % 8 || ld_src % 8 || ld_dst % 8 || !aligned16(src)) return MGF_ERR_ALIGNMENT;
+  unsigned int* status = status_word_address();
+  if (status == nullptr) return MGF_ERR_CUDA;
   push_rows_kernel<<<grid_for(n_max), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), ld_src, src_idx, scale, n_max, n_dev, dst_rank, dst_row, peer_bases,
-      world, dst_rows, ld_dst, row_elems / 8);
+      world, dst_rows, ld_dst, row_elems / 8, n_src, status);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 

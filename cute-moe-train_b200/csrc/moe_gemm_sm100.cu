@@ -1112,6 +1112,16 @@ extern "C" const char* mgf_status_string(int status) {
   }
 }
 
+namespace mgf {
+// Device address of g_status on the current device, for the kernels of the other translation units
+// (the expert-parallel row movement) that report into the same word.
+unsigned int* status_word_address() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+  return static_cast<unsigned int*>(p);
+}
+}  // namespace mgf
+
 extern "C" int mgf_device_status(int device, uint32_t* status_out, int clear) {
   int prev = 0;
   if (cudaGetDevice(&prev) != cudaSuccess) return MGF_ERR_CUDA;
@@ -1364,8 +1374,10 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
 //  * every call shares the one array and it keeps the last call's contents, so each call clears the
 //    word it uses (cudaMemsetAsync on `stream`) before the kernel; calls that overlap on the GPU
 //    (different streams, no ordering between them) race on the counter and must not be issued;
-//  * the first call on a device looks up the array's device address (cudaGetSymbolAddress with that
-//    device current) and caches it; make that first call before any stream capture.
+//  * each call looks up the array's device address afresh (cudaGetSymbolAddress with the calling
+//    device current), so the address stays right after a cudaDeviceReset reloads the module; while
+//    `stream` is capturing no lookup is made and the last address found on that device is reused,
+//    so make the first call on each device before any stream capture.
 //  * nothing here calls cudaMalloc, cudaFree or any allocating routine.
 
 namespace mgf {
@@ -1373,22 +1385,21 @@ namespace mgf {
 constexpr int kNoAllocScratchWords = 64;
 static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchWords];
 
-static int32_t* noalloc_scratch_address(int dev) {
+static int32_t* noalloc_scratch_address(int dev, bool capturing) {
   static int32_t* cached[64] = {};
   static std::mutex mu;
   if (dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> g(mu);
-  if (cached[dev] == nullptr) {
-    // The symbol's host-side name is only a stand-in: the device address must come from the
-    // runtime, with this device current.
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) {
-      record_error("cudaGetSymbolAddress(g_noalloc_scratch)", e);
-      return nullptr;
-    }
-    cached[dev] = static_cast<int32_t*>(ptr);
+  if (capturing) return cached[dev];  // no runtime lookups inside a capture
+  // The symbol's host-side name is only a stand-in: the device address must come from the
+  // runtime, with this device current.
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) {
+    record_error("cudaGetSymbolAddress(g_noalloc_scratch)", e);
+    return nullptr;
   }
+  cached[dev] = static_cast<int32_t*>(ptr);
   return cached[dev];
 }
 
@@ -1416,9 +1427,16 @@ extern "C" int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* 
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MGF_ERR_CUDA;
-  int32_t* scratch = noalloc_scratch_address(dev);
-  if (scratch == nullptr) return MGF_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return MGF_ERR_CUDA;
+  int32_t* scratch = noalloc_scratch_address(dev, cap != cudaStreamCaptureStatusNone);
+  if (scratch == nullptr) {
+    if (g_last_error[0] == 0)
+      snprintf(g_last_error, sizeof(g_last_error),
+               "mgf_grouped_gemm_launch_noalloc: first call on this device made during stream capture");
+    return MGF_ERR_CUDA;
+  }
   const cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(int32_t) * words_needed, st);
   if (e != cudaSuccess) {
     record_error("cudaMemsetAsync(static scratch)", e);

@@ -546,7 +546,7 @@ Tensor gather_rows_cuda(const Tensor& src, const Tensor& idx_in, const std::opti
     scale = scale_in->to(at::kFloat).contiguous();
     TORCH_CHECK(scale.numel() == idx.numel(), "gather_rows: scale must have one entry per row");
   }
-  check_launch(mgf_gather_rows(src.data_ptr(), src.stride(0), idx.data_ptr<int64_t>(),
+  check_launch(mgf_gather_rows(src.data_ptr(), src.stride(0), src.size(0), idx.data_ptr<int64_t>(),
                                scale.defined() ? scale.data_ptr<float>() : nullptr, idx.numel(), src.size(1),
                                out.data_ptr(), out.stride(0), at::cuda::getCurrentCUDAStream().stream()),
                "gather_rows");
@@ -565,7 +565,7 @@ Tensor combine_rows_cuda(const Tensor& rows, const Tensor& pos_in, const std::op
     w = w_in->to(at::kFloat).contiguous();
     TORCH_CHECK(w.numel() == pos.numel(), "combine_rows: one weight per (row, slot)");
   }
-  check_launch(mgf_combine_rows(rows.data_ptr(), rows.stride(0), pos.data_ptr<int64_t>(),
+  check_launch(mgf_combine_rows(rows.data_ptr(), rows.stride(0), rows.size(0), pos.data_ptr<int64_t>(),
                                 w.defined() ? w.data_ptr<float>() : nullptr, n_out, static_cast<int32_t>(k),
                                 rows.size(1), out.data_ptr(), out.stride(0), at::cuda::getCurrentCUDAStream().stream()),
                "combine_rows");
@@ -600,7 +600,7 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
     TORCH_CHECK(n_dev->scalar_type() == at::kInt && n_dev->numel() >= 1, "push_rows: n_dev must be int32");
     nd = n_dev->data_ptr<int32_t>();
   }
-  check_launch(mgf_push_rows(src.data_ptr(), src.stride(0), si, sc, n_max, nd, dst_rank.data_ptr<int64_t>(),
+  check_launch(mgf_push_rows(src.data_ptr(), src.stride(0), src.size(0), si, sc, n_max, nd, dst_rank.data_ptr<int64_t>(),
                              dst_row.data_ptr<int64_t>(),
                              reinterpret_cast<const unsigned long long*>(peer_bases.data_ptr<int64_t>()),
                              peer_bases.numel(), dst_rows, ld_dst, src.size(1),

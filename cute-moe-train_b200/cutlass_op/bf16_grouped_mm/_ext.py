@@ -20,6 +20,7 @@ OPS_PATH = _HERE / "_grouped_mm_ops.so"
 # Device status bits (include/moe_gemm.h).
 DEV_WAIT_TIMEOUT = 0x1
 DEV_BAD_OFFS = 0x2
+DEV_ROW_OUT_OF_RANGE = 0x4
 
 
 def _require(path: Path) -> None:
@@ -93,6 +94,8 @@ def check_device_status(device: int | None = None) -> None:
             what.append("a pipeline wait ran out and the kernel stopped early")
         if st & DEV_BAD_OFFS:
             what.append("offs was not non-decreasing within [0, total rows]")
+        if st & DEV_ROW_OUT_OF_RANGE:
+            what.append("a gather/combine/push row index fell outside its buffer (row skipped)")
         raise RuntimeError("grouped_mm device status: " + "; ".join(what))
 
 

@@ -119,7 +119,8 @@ def make_weights_device(shape: MoEShape, seed: int, device, dtype=torch.bfloat16
 
 
 def config1(device="cpu"):
-    """BASELINE config 1, generated in the order x, W_up, b_up, W_down, b_down from seed 0."""
+    """Config 1 (E=8, H=2048, I=1024, the reference quick-start token counts), generated in the
+    order x, W_up, b_up, W_down, b_down from seed 0."""
     E, H, I = 8, 2048, 1024
     g = torch.Generator(device="cpu").manual_seed(0)
     counts = torch.tensor(CONFIG1_TPE, dtype=torch.int64)

@@ -55,6 +55,8 @@ enum mgf_status {
 /* Device status bits recorded by the kernels (read with mgf_device_status). */
 #define MGF_DEV_WAIT_TIMEOUT 0x1u  /* a pipeline wait ran out; the kernel stopped early        */
 #define MGF_DEV_BAD_OFFS 0x2u      /* offs not non-decreasing or beyond the row extent; clamped */
+#define MGF_DEV_ROW_OUT_OF_RANGE 0x4u /* a row index of gather/combine/push fell outside its buffer;
+                                         that row was skipped (left unwritten)                    */
 
 /*
  * One grouped GEMM.  Matrix layouts are given as element strides of bf16 tensors.
@@ -132,8 +134,9 @@ int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream);
  * desc->workspace comes instead from a 256-byte static device array inside the library (64 int32
  * words, 1 used per call; held by every GPU that loads the library until exit).  desc->workspace
  * must be NULL.  The call clears the word it uses on `stream` before the kernel; all calls share
- * the array, so calls that overlap on the GPU race and must not be issued.  The first call on a
- * device looks up the array's address and should come before any stream capture.  Allocates
+ * the array, so calls that overlap on the GPU race and must not be issued.  Each call looks up
+ * the array's address on the calling device (so it stays right after a device reset); the first
+ * call on a device should come before any stream capture.  Allocates
  * nothing (no cudaMalloc/cudaFree).  Same return codes as mgf_grouped_gemm_launch. */
 int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* stream);
 
@@ -142,22 +145,25 @@ int mgf_grouped_gemm_launch_noalloc(const mgf_gemm_desc* desc, void* stream);
  * 16-byte aligned bases, int64 device index arrays, optional fp32 device scales (NULL = 1).
  *   mgf_gather_rows:  dst[i] = scale[i] * src[idx[i]],                     i < n_rows
  *   mgf_combine_rows: out[t] = sum_{j<k} weights[t*k+j] * rows[pos[t*k+j]], t < n_out (fp32 sum)
+ * n_src / n_rows is the row count of src / rows: an index outside [0, n_src) leaves its output
+ * row unwritten (combine: any of the token's k indices) and sets MGF_DEV_ROW_OUT_OF_RANGE.
  * Dispatch gathers token copies into expert order; combine sums each token's k expert outputs;
  * each is the other's backward. */
-int mgf_gather_rows(const void* src, int64_t ld_src, const int64_t* idx, const float* scale, int64_t n_rows,
-                    int64_t row_elems, void* dst, int64_t ld_dst, void* stream);
-int mgf_combine_rows(const void* rows, int64_t ld_rows, const int64_t* pos, const float* weights, int64_t n_out,
-                     int32_t k, int64_t row_elems, void* out, int64_t ld_out, void* stream);
+int mgf_gather_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* idx, const float* scale,
+                    int64_t n_rows, int64_t row_elems, void* dst, int64_t ld_dst, void* stream);
+int mgf_combine_rows(const void* rows, int64_t ld_rows, int64_t n_rows, const int64_t* pos, const float* weights,
+                     int64_t n_out, int32_t k, int64_t row_elems, void* out, int64_t ld_out, void* stream);
 
 /* Expert-parallel push over NVLink peer memory (no counterpart in the reference): for i < n rows
  * (n = n_max, or *n_dev when n_dev is non-NULL -- a device-side count), write
  * scale[i] * src[src_idx[i]] (src_idx NULL = i, scale NULL = 1) to row dst_row[i] of the buffer at
  * peer_bases[dst_rank[i]] (device array of `world` base addresses, one per rank, from CUDA IPC
  * mappings; each buffer dst_rows rows of stride ld_dst).  Rows whose rank or destination row falls
- * outside [0, world) x [0, dst_rows) are skipped.  Plain peer stores, no multicast; the caller
- * orders them before the readers with a stream-ordered barrier. */
-int mgf_push_rows(const void* src, int64_t ld_src, const int64_t* src_idx, const float* scale, int64_t n_max,
-                  const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
+ * outside [0, world) x [0, dst_rows), or whose source row falls outside [0, n_src), are skipped and
+ * set MGF_DEV_ROW_OUT_OF_RANGE.  Plain peer stores, no multicast; the caller orders them before
+ * the readers with a stream-ordered barrier. */
+int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* src_idx, const float* scale,
+                  int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
                   const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
                   int64_t row_elems, void* stream);
 

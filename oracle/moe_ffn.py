@@ -15,8 +15,8 @@ cutlass_op/bf16_grouped_mm/), both in float32 torch on the CPU over bf16-rounded
                           grad_aux = bf16(SwiGLU_bwd(g@W_down^T, aux))         csrc/grouped_mm_swiglu_bwd_visitor.cuh:35-68
                           dx = bf16(grad_aux@W_up^T), dW_up = bf16(x^T grad_aux),
                           db_up = bf16(sum grad_aux)                            custom_op.py:508-518
-``fp32_composition``  BASELINE config 1's primary oracle: a plain per-expert fp32 composition
-                  (matmul + bias + clamp + sigmoid) differentiated by torch autograd, with no
+``fp32_composition``  the primary oracle of the E=8, H=2048, I=1024 CPU case: a plain per-expert
+                  fp32 composition (matmul + bias + clamp + sigmoid) differentiated by torch autograd, with no
                   intermediate rounding.
 
 Parity pin: the reference ships no tests or golden vectors.  tests/golden/make_golden.py runs the

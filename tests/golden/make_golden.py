@@ -7,9 +7,9 @@ reads it):
 
 It loads Butterfingrz/CuTe-MoE-Train's ``cutlass_op/bf16_grouped_mm/__init__.py`` and
 ``custom_op.py`` unmodified under the module name ``ref_bf16_grouped_mm`` and injects a CPU
-stand-in for its compiled ``_ext`` module.  The reference's autograd routing, fused-only contract,
-ZeroTensor handling and ``_segment_sum_rows`` therefore run as written; only the three CUDA entry
-points are restated here, with the reference kernels' arithmetic:
+stand-in for its compiled ``_ext`` module (oracle/ref_ext_cpu.py).  The reference's autograd
+routing, fused-only contract, ZeroTensor handling and ``_segment_sum_rows`` therefore run as
+written; only the three CUDA entry points are restated, with the reference kernels' arithmetic:
 
 * ``_grouped_mm_cuda``: fp32 accumulate + bias, one bf16 rounding (csrc/grouped_mm_kernel.cuh:130-143);
   ragged-K outputs of empty groups are written as zeros.
@@ -24,15 +24,14 @@ process that also loads this repository's native operators.
 
 from __future__ import annotations
 
-import importlib.util
 import math
 import sys
-import types
 from pathlib import Path
 
 import torch
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent.parent))  # the repository root, for oracle/
 OUT = HERE / "moe_ffn_golden.pt"
 
 CASES = [
@@ -45,98 +44,10 @@ CASES = [
 ]
 
 
-def _bf(t):
-    return t.to(torch.bfloat16)
-
-
-def _segments(offs):
-    prev = 0
-    for e, end in enumerate(offs.tolist()):
-        yield e, prev, int(end)
-        prev = int(end)
-
-
-def _stub_ext():
-    m = types.ModuleType("ref_bf16_grouped_mm._ext")
-
-    def _grouped_mm_cuda(mat_a, mat_b, offs, bias, out_dtype):
-        a2, b2 = mat_a.dim() == 2, mat_b.dim() == 2
-        if a2 and not b2:
-            n = mat_b.shape[-1]
-            out = torch.zeros(mat_a.shape[0], n, dtype=torch.bfloat16)
-            for e, s, t in _segments(offs):
-                if t > s:
-                    y = mat_a[s:t].float() @ mat_b[e].float()
-                    if bias is not None:
-                        y = y + bias[e].float()
-                    out[s:t] = _bf(y)
-            return out
-        if a2 and b2:
-            E = offs.numel()
-            out = torch.zeros(E, mat_a.shape[0], mat_b.shape[1], dtype=torch.bfloat16)
-            for e, s, t in _segments(offs):
-                if t > s:
-                    out[e] = _bf(mat_a[:, s:t].float() @ mat_b[s:t].float())
-            return out
-        y = mat_a.float() @ mat_b.float()
-        if bias is not None:
-            y = y + bias.float().unsqueeze(-2)
-        return _bf(y)
-
-    def _grouped_mm_swiglu_cuda(mat_a, mat_b, offs, bias, aux_out, swiglu_out, alpha, limit, store_aux):
-        aux = _grouped_mm_cuda(mat_a, mat_b, offs, bias, None)
-        if store_aux:
-            aux_out.copy_(aux)
-        bf = torch.bfloat16
-        g = aux[:, 0::2]
-        u = aux[:, 1::2]
-        lim = torch.tensor(limit).to(bf)
-        g = torch.minimum(g, lim)
-        u = torch.maximum(torch.minimum(u, lim), -lim)
-        ag = _bf(torch.tensor(alpha * 0.5).to(bf).float() * g.float())
-        t = _bf(torch.tanh(ag.float()))
-        s = _bf(t.float() * 0.5 + 0.5)
-        gs = _bf(g.float() * s.float())
-        res = _bf(gs.float() * u.float() + gs.float())
-        rows = int(offs[-1]) if offs.numel() else 0
-        swiglu_out[:rows] = res[:rows]
-
-    def _grouped_mm_swiglu_bwd_cuda(grad_output, down_w_t, offs, aux_packed, grad_packed, alpha, limit):
-        aux = aux_packed.view(torch.bfloat16).float()
-        grad = grad_packed.view(torch.bfloat16)
-        for e, s, t in _segments(offs):
-            if t <= s:
-                continue
-            gs = grad_output[s:t].float() @ down_w_t[e].float()
-            gate = aux[s:t, 0::2]
-            up = aux[s:t, 1::2]
-            gc = torch.clamp(gate, max=limit)
-            uc = torch.clamp(up, min=-limit, max=limit)
-            sig = 0.5 * torch.tanh(0.5 * alpha * gc) + 0.5
-            glu = gc * sig
-            dg = gs * (uc + 1.0) * sig * (1.0 + alpha * gc * (1.0 - sig))
-            du = gs * glu
-            dg = dg * (gate <= limit).float()
-            du = du * ((up >= -limit) & (up <= limit)).float()
-            grad[s:t, 0::2] = _bf(dg)
-            grad[s:t, 1::2] = _bf(du)
-
-    m._grouped_mm_cuda = _grouped_mm_cuda
-    m._grouped_mm_swiglu_cuda = _grouped_mm_swiglu_cuda
-    m._grouped_mm_swiglu_bwd_cuda = _grouped_mm_swiglu_bwd_cuda
-    return m
-
-
 def load_reference(ref_root: Path):
-    pkg_dir = ref_root / "cutlass_op" / "bf16_grouped_mm"
-    sys.modules["ref_bf16_grouped_mm._ext"] = _stub_ext()
-    spec = importlib.util.spec_from_file_location(
-        "ref_bf16_grouped_mm", pkg_dir / "__init__.py", submodule_search_locations=[str(pkg_dir)]
-    )
-    mod = importlib.util.module_from_spec(spec)
-    sys.modules["ref_bf16_grouped_mm"] = mod
-    spec.loader.exec_module(mod)
-    return mod
+    from oracle.ref_ext_cpu import load_reference_layer
+
+    return load_reference_layer(ref_root / "cutlass_op" / "bf16_grouped_mm")
 
 
 def make_inputs(E, H, I, counts, seed, grad):

@@ -43,19 +43,15 @@ def test_null_descriptor_rejected():
 
 
 def test_ctypes_descriptor_layouts_match_the_library():
-    """The ctypes mirrors of mgf_gemm_desc (the INTEGRATION stub and the no-alloc test's) have the
-    size the library was compiled with."""
+    """The ctypes mirrors of mgf_gemm_desc (the reference-side binding ctypes_ext.py and the no-alloc
+    test's) have the size the library was compiled with."""
     import importlib.util
 
     lib = ctypes.CDLL(str(LIB))
     lib.mgf_gemm_desc_size.restype = ctypes.c_size_t
-    spec = importlib.util.spec_from_file_location("t_no_alloc", REPO / "tests" / "test_zz_no_alloc.py")
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
-    assert ctypes.sizeof(mod.MgfGemmDesc) == lib.mgf_gemm_desc_size()
-    stub = (REPO / "INTEGRATION.md").read_text()
-    block = stub[stub.index("class MgfGemmDesc(ctypes.Structure):"):]
-    block = block[: block.index("\n\n")]
-    ns = {"ctypes": ctypes}
-    exec(block, ns)  # the documented stub, as a maintainer would paste it
-    assert ctypes.sizeof(ns["MgfGemmDesc"]) == lib.mgf_gemm_desc_size()
+    for name, path in (("t_no_alloc", REPO / "tests" / "test_zz_no_alloc.py"),
+                       ("t_ctypes_ext", REPO / "cute-moe-train_b200" / "ctypes_ext.py")):
+        spec = importlib.util.spec_from_file_location(name, path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)  # ctypes_ext also checks its own layout at import
+        assert ctypes.sizeof(mod.MgfGemmDesc) == lib.mgf_gemm_desc_size(), name

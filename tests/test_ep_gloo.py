@@ -204,3 +204,36 @@ def test_push_plan_is_a_consistent_exchange(world, E, T, K):
             assert e // el == o
             keys.append((e, s, p))
         assert keys == sorted(keys)
+
+
+def test_ep_oracle_matches_direct_autograd():
+    """oracle.ep_ffn.ep_reference (the checker of the GPU expert-parallel tests) against a direct
+    fp32 per-token autograd computation over two ranks' tokens."""
+    from oracle import moe_ffn as O
+    from oracle.ep_ffn import ep_reference
+    from cutlass_op.bf16_grouped_mm.expert_parallel import route_tokens
+
+    bf = torch.bfloat16
+    wts = [t.to(bf) for t in _weights()]
+    xs, idxs, ws, gs = [], [], [], []
+    for r in range(2):
+        g = torch.Generator().manual_seed(300 + r)
+        xs.append(torch.randn(T, H, generator=g).to(bf))
+        idxs.append(route_tokens(T, E, K, "zipf", seed=40 + r))
+        ws.append(torch.rand(T, K, generator=g))
+        gs.append(torch.randn(T, H, generator=g).to(bf))
+    want = ep_reference(xs, idxs, ws, gs, *wts)
+    leaves = [t.float().requires_grad_(True) for t in wts]
+    for r in range(2):
+        x = xs[r].float().requires_grad_(True)
+        w = ws[r].clone().requires_grad_(True)
+        out = torch.stack([sum(w[t, j] * _ffn(x[t:t + 1], int(idxs[r][t, j]), *leaves)[0] for j in range(K))
+                           for t in range(T)])
+        (out * gs[r].float()).sum().backward()
+        for name, a, b in (("out", want["out"][r], out.detach()), ("dx", want["dx"][r], x.grad),
+                           ("dw_router", want["dw_router"][r], w.grad)):
+            res = O.check(f"rank{r}:{name}", a, b)
+            assert res["ok"], res
+    for name, p in zip(("dw_up", "db_up", "dw_down", "db_down"), leaves):
+        res = O.check(name, want[name], p.grad)
+        assert res["ok"], res

@@ -15,37 +15,41 @@ pytestmark = pytest.mark.gpu
 E, H, I, T, K = 8, 256, 128, 300, 4
 
 
-def _reference_ffn(x, idx, wu, bu, wd, bd):
-    """Non-EP oracle: every routed copy through its expert (kernel_chain rounding), summed per token."""
-    flat = idx.reshape(-1)
-    order = torch.argsort(flat, stable=True)
-    counts = torch.bincount(flat, minlength=wu.shape[0])
-    offs = torch.cumsum(counts, 0).to(torch.int32)
-    rows = x[torch.div(order, idx.shape[1], rounding_mode="floor")]
-    g = torch.zeros(rows.shape[0], wd.shape[-1], dtype=torch.bfloat16)
-    ref = O.kernel_chain(rows, wu, bu, wd, bd, offs, g)
-    y = ref["out"]
-    out = torch.zeros(x.shape[0], x.shape[1]).index_add(0, torch.div(order, idx.shape[1], rounding_mode="floor"), y)
-    return out
+def _check_ep(tag, got, want, rank, e_local):
+    """got: this rank's (out, dx, dw_router, dw_up, db_up, dw_down, db_down); want: ep_reference()."""
+    sl = slice(rank * e_local, (rank + 1) * e_local)
+    pairs = [("out", got[0], want["out"][rank]), ("dx", got[1], want["dx"][rank]),
+             ("dw_router", got[2], want["dw_router"][rank]), ("dw_up", got[3], want["dw_up"][sl]),
+             ("db_up", got[4], want["db_up"][sl]), ("dw_down", got[5], want["dw_down"][sl]),
+             ("db_down", got[6], want["db_down"][sl])]
+    for name, a, b in pairs:
+        r = O.check(f"{tag}:rank{rank}:{name}", torch.as_tensor(a).float(), b.float())
+        assert r["ok"], r
 
 
 def test_ep_world1_matches_oracle():
+    """One rank: outputs, token and router-weight gradients and all four weight/bias gradients
+    against the single-process oracle, with router weights and a random output gradient."""
     from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+    from oracle.ep_ffn import ep_reference
 
     dev = torch.device("cuda", 0)
     ffn = EPMoEFFN(E, H, I, device=dev, seed=5)
-    x = torch.randn(T, H, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w = torch.rand(T, K, generator=g)
+    gout = torch.randn(T, H, generator=g).to(torch.bfloat16)
     idx = route_tokens(T, E, K, "zipf", seed=2)
     xd = x.to(dev).requires_grad_(True)
-    out = ffn(xd, idx.to(dev))
-    out.float().sum().backward()
+    wd = w.to(dev).requires_grad_(True)
+    out = ffn(xd, idx.to(dev), wd)
+    out.backward(gout.to(dev))
     torch.cuda.synchronize()
-    ref = _reference_ffn(x, idx, ffn.w_up.detach().cpu(), ffn.b_up.detach().cpu(), ffn.w_down.detach().cpu(),
-                         ffn.b_down.detach().cpu())
-    r = O.check("ep_out", out.float().cpu(), ref)
-    assert r["ok"], r
-    for p in (xd.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad, ffn.b_down.grad):
-        assert p is not None and torch.isfinite(p.float()).all()
+    want = ep_reference([x], [idx], [w], [gout], *[p.detach().cpu() for p in
+                                                    (ffn.w_up, ffn.b_up, ffn.w_down, ffn.b_down)])
+    got = [t.detach().cpu() for t in (out, xd.grad, wd.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad,
+                                      ffn.b_down.grad)]
+    _check_ep("world1", got, want, 0, E)
 
 
 def _free_port():
@@ -54,75 +58,6 @@ def _free_port():
     p = s.getsockname()[1]
     s.close()
     return p
-
-
-def _ep_worker(rank, world, port, q):
-    try:
-        _ep_worker_body(rank, world, port, q)
-    except Exception:  # report instead of leaving the parent waiting
-        import traceback
-
-        q.put((rank, "error", traceback.format_exc()))
-
-
-def _ep_worker_body(rank, world, port, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    from conftest import PKG  # noqa: F401
-
-    import torch.distributed as dist
-
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
-    try:
-        from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
-
-        ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport="nccl")
-        x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
-        idx = route_tokens(T, E, K, "uniform", seed=20 + rank)
-        out = ffn(x.to(dev), idx.to(dev))
-        torch.cuda.synchronize()
-        # gather every rank's weights so rank 0 can check against a single-process oracle
-        ws = [p.detach() for p in (ffn.w_up, ffn.b_up, ffn.w_down, ffn.b_down)]
-        gathered = []
-        for w in ws:
-            parts = [torch.empty_like(w) for _ in range(world)]
-            dist.all_gather(parts, w)
-            gathered.append(torch.cat(parts, 0).cpu().float().numpy())
-        q.put((rank, x.float().numpy(), idx.numpy(), out.detach().float().cpu().numpy(), gathered))
-    finally:
-        dist.destroy_process_group()
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_world2_nccl_matches_oracle():
-    import torch.multiprocessing as mp
-
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = {}
-    try:
-        for _ in range(2):
-            r = q.get(timeout=240)
-            assert not (isinstance(r[1], str) and r[1] == "error"), r[2]
-            res[r[0]] = r
-    finally:
-        for p in procs:
-            p.join(timeout=60)
-            if p.is_alive():
-                p.kill()
-    for p in procs:
-        assert p.exitcode == 0
-    for rank in range(2):
-        _, x, idx, out, ws = res[rank]
-        wts = [torch.from_numpy(w).to(torch.bfloat16) for w in ws]
-        ref = _reference_ffn(torch.from_numpy(x).to(torch.bfloat16), torch.from_numpy(idx), *wts)
-        r = O.check(f"ep_out_rank{rank}", torch.from_numpy(out), ref)
-        assert r["ok"], r
 
 
 def test_row_kernels_match_torch():
@@ -141,6 +76,48 @@ def test_row_kernels_match_torch():
     ref = (src[pos].float() * w.unsqueeze(1)).view(20, k, -1).sum(1)
     r = O.check("combine", out.float().cpu(), ref.cpu())
     assert r["ok"], r
+
+
+def test_row_kernels_flag_out_of_range_index():
+    """An index outside the source rows is skipped, its output row keeps its old contents, the
+    other rows are right, and MGF_DEV_ROW_OUT_OF_RANGE is recorded (read and cleared)."""
+    import ctypes
+
+    from cutlass_op.bf16_grouped_mm import _ext
+
+    lib = _ext.lib
+    _ext.device_status(clear=True)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = torch.Generator().manual_seed(11)
+    src = torch.randn(40, 64, generator=g).to(torch.bfloat16).cuda()
+    idx = torch.tensor([3, 39, 40, 0, -1, 7], dtype=torch.int64).cuda()   # 40 and -1 are outside
+    dst = torch.full((6, 64), 5.0, dtype=torch.bfloat16).cuda()
+    rc = lib.mgf_gather_rows(ctypes.c_void_p(src.data_ptr()), ctypes.c_int64(64), ctypes.c_int64(40),
+                             ctypes.c_void_p(idx.data_ptr()), None, ctypes.c_int64(6), ctypes.c_int64(64),
+                             ctypes.c_void_p(dst.data_ptr()), ctypes.c_int64(64), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    good = [0, 1, 3, 5]
+    assert torch.equal(dst[good], src[idx[good]])
+    assert (dst[[2, 4]].float() == 5.0).all()
+    assert _ext.device_status(clear=True) == _ext.DEV_ROW_OUT_OF_RANGE
+    # combine: a token with one bad slot is left untouched, the others are summed
+    k = 2
+    pos = torch.tensor([0, 1, 2, 99, 4, 5], dtype=torch.int64).cuda()
+    out = torch.full((3, 64), 5.0, dtype=torch.bfloat16).cuda()
+    rc = lib.mgf_combine_rows(ctypes.c_void_p(src.data_ptr()), ctypes.c_int64(64), ctypes.c_int64(40),
+                              ctypes.c_void_p(pos.data_ptr()), None, ctypes.c_int64(3), ctypes.c_int32(k),
+                              ctypes.c_int64(64), ctypes.c_void_p(out.data_ptr()), ctypes.c_int64(64), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = (src[[0, 4]].float() + src[[1, 5]].float()).to(torch.bfloat16)
+    assert torch.equal(out[[0, 2]], ref)
+    assert (out[1].float() == 5.0).all()
+    assert _ext.device_status(clear=True) == _ext.DEV_ROW_OUT_OF_RANGE
+    with pytest.raises(RuntimeError, match="outside its buffer"):
+        torch.ops.grouped_mm.gather_rows(src, idx, None)
+        _ext.check_device_status()
+    assert _ext.device_status(clear=True) == 0
 
 
 def test_ep_autograd_row_functions():
@@ -179,22 +156,34 @@ def _transport_worker(rank, world, port, q):
             from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
             res = {}
+            gen = torch.Generator().manual_seed(10 + rank)
+            x0 = torch.randn(T, H, generator=gen).to(torch.bfloat16)
+            w0 = torch.rand(T, K, generator=gen)
+            g0 = torch.randn(T, H, generator=gen).to(torch.bfloat16)
+            idx = route_tokens(T, E, K, "zipf", seed=20 + rank)
+            res["inputs"] = [x0.float().numpy(), idx.numpy(), w0.numpy(), g0.float().numpy()]
             for transport in ("nccl", "peer", "peer_overlap"):
                 ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport.split("_")[0],
                                overlap=transport.endswith("overlap"))
-                x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
-                x = x.to(dev).requires_grad_(True)
-                idx = route_tokens(T, E, K, "zipf", seed=20 + rank).to(dev)
-                w = torch.rand(T, K, generator=torch.Generator().manual_seed(30 + rank)).to(dev)
-                for step in range(2):  # second step reuses the peer buffers
+                x = x0.to(dev).requires_grad_(True)
+                w = w0.to(dev).requires_grad_(True)
+                for step in range(2):  # the second step reuses the peer buffers
                     x.grad = None
+                    w.grad = None
                     ffn.zero_grad()
-                    out = ffn(x, idx, w)
-                    g = torch.randn(T, H, generator=torch.Generator().manual_seed(40 + rank + step)).to(torch.bfloat16)
-                    out.backward(g.to(dev))
+                    out = ffn(x, idx.to(dev), w)
+                    out.backward(g0.to(dev))
                 torch.cuda.synchronize()
                 res[transport] = [t.detach().float().cpu().numpy() for t in
-                                  (out, x.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad, ffn.b_down.grad)]
+                                  (out, x.grad, w.grad, ffn.w_up.grad, ffn.b_up.grad, ffn.w_down.grad,
+                                   ffn.b_down.grad)]
+            # every rank's expert weights, so the parent can build the single-process oracle
+            gathered = []
+            for p in (ffn.w_up, ffn.b_up, ffn.w_down, ffn.b_down):
+                parts = [torch.empty_like(p) for _ in range(world)]
+                dist.all_gather(parts, p.detach().contiguous())
+                gathered.append(torch.cat(parts, 0).float().cpu().numpy())
+            res["weights"] = gathered
             q.put((rank, res))
         finally:
             dist.destroy_process_group()
@@ -205,10 +194,14 @@ def _transport_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_world2_peer_transport_matches_nccl():
-    """Dispatch/combine as peer-memory pushes gives the NCCL all-to-all path's outputs and gradients;
-    with the dispatch-gradient push overlapped, bit-identical ones."""
+def test_ep_world2_every_transport_matches_oracle():
+    """Two ranks, Zipf routing, router weights, a random output gradient, two steps: for the NCCL
+    all-to-all, the peer pushes and the peer pushes with the overlapped dispatch gradient, each
+    rank's output, token gradient, router-weight gradient and its experts' weight and bias gradients
+    match the single-process oracle over both ranks' tokens; the overlap changes no bit."""
     import torch.multiprocessing as mp
+
+    from oracle.ep_ffn import ep_reference
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -227,11 +220,15 @@ def test_ep_world2_peer_transport_matches_nccl():
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    names = ["out", "dx", "dw_up", "db_up", "dw_down", "db_down"]
+    for p in procs:
+        assert p.exitcode == 0
+    bf = torch.bfloat16
+    ins = [res[r]["inputs"] for r in range(2)]
+    wts = [torch.from_numpy(a).to(bf) for a in res[0]["weights"]]
+    want = ep_reference([torch.from_numpy(i[0]).to(bf) for i in ins], [torch.from_numpy(i[1]) for i in ins],
+                        [torch.from_numpy(i[2]) for i in ins], [torch.from_numpy(i[3]).to(bf) for i in ins], *wts)
     for rank in range(2):
-        for name, a, b in zip(names, res[rank]["peer"], res[rank]["nccl"]):
-            r = O.check(f"rank{rank}:{name}", torch.from_numpy(a), torch.from_numpy(b))
-            assert r["ok"], r
-        # the overlapped dispatch-gradient push changes the timing, not one bit of the results
-        for name, a, b in zip(names, res[rank]["peer_overlap"], res[rank]["peer"]):
-            assert (a == b).all(), f"rank{rank}:{name}: overlap changed the result"
+        for transport in ("nccl", "peer", "peer_overlap"):
+            _check_ep(transport, [torch.from_numpy(a) for a in res[rank][transport]], want, rank, E // 2)
+        for a, b in zip(res[rank]["peer_overlap"], res[rank]["peer"]):
+            assert (a == b).all(), f"rank{rank}: overlap changed the result"

@@ -212,3 +212,35 @@ def test_reference_binding_functions_match_the_operators():
     assert torch.equal(g_packed.view(torch.bfloat16)[:rows], g_ref[:rows])
     out = _ext._grouped_mm_cuda(s_ref, w_down.cuda(), offs, None, None)
     assert torch.equal(out[:rows], m.grouped_mm(s_ref, w_down.cuda(), offs)[:rows])
+
+
+def test_rows_past_offs_end_are_never_written():
+    """offs[-1] < rows of the buffers: the in-place binding functions leave every row at or past
+    offs[-1] untouched (NaN-prefilled here) in swiglu_out, aux_out and the packed grad_aux."""
+    m = _lib()
+    from cutlass_op.bf16_grouped_mm import _ext
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(3, 128, 64, [70, 0, 131], seed=23)
+    M, I = x.shape[0] + 77, w_up.shape[2] // 2    # 77 rows past offs[-1]
+    xp = torch.cat([x, torch.randn(77, x.shape[1]).to(torch.bfloat16)]).cuda()
+    gp = torch.cat([gout, torch.randn(77, gout.shape[1]).to(torch.bfloat16)]).cuda()
+    w_up, b_up, w_down, offs = (t.cuda() for t in (w_up, b_up, w_down, offs))
+    rows = int(offs[-1])
+    nan = float("nan")
+    s_out = torch.full((M, I), nan, dtype=torch.bfloat16, device="cuda")
+    aux_out = torch.full((M, 2 * I), nan, dtype=torch.bfloat16, device="cuda")
+    _ext._grouped_mm_swiglu_cuda(xp, w_up, offs, b_up, aux_out, s_out, 1.702, 7.0, True)
+    g_packed = torch.full((M, I), nan, dtype=torch.float32, device="cuda")
+    _ext._grouped_mm_swiglu_bwd_cuda(gp, w_down.transpose(-2, -1), offs, aux_out.view(torch.float32), g_packed,
+                                     1.702, 7.0)
+    torch.cuda.synchronize()
+    m.check_device_status()
+    assert torch.isnan(s_out[rows:].float()).all() and torch.isnan(aux_out[rows:].float()).all()
+    assert torch.isnan(g_packed.view(torch.bfloat16)[rows:].float()).all()
+    assert not torch.isnan(s_out[:rows].float()).any() and not torch.isnan(aux_out[:rows].float()).any()
+    assert not torch.isnan(g_packed.view(torch.bfloat16)[:rows].float()).any()
+    ref = O.kernel_chain(x, *(t.cpu() for t in (w_up, b_up, w_down)), b_down, offs.cpu(), gout)
+    for name, got in (("swiglu_out", s_out), ("aux", aux_out), ("grad_aux", g_packed.view(torch.bfloat16))):
+        r = O.check(name, got[:rows].float().cpu(), ref[name][:rows])
+        assert r["ok"], r

@@ -74,3 +74,32 @@ def test_checker_uses_float64_cosine():
     a = torch.randn(1 << 16)
     assert O.cosine(a, a) == pytest.approx(1.0, abs=1e-12)
     assert O.cosine(a, a) <= 1.0 + 1e-12
+
+
+def test_staged_reference_layer_reproduces_golden(golden):
+    """The staged copy of the reference's Python layer (baseline/_ref), run over the CPU stand-in of its
+    kernels in a child process, reproduces the committed fixtures bit for bit."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    staged = repo / "baseline" / "_ref" / "group_gemm"
+    if not (staged / "custom_op.py").is_file():
+        pytest.skip("reference layer not staged (baseline/_ref)")
+    child = (
+        "import sys, torch; sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + '/tests/golden')\n"
+        "from oracle.ref_ext_cpu import load_reference_layer\n"
+        "import make_golden as mg\n"
+        "ref = load_reference_layer(sys.argv[2])\n"
+        "g = torch.load(sys.argv[1] + '/tests/golden/moe_ffn_golden.pt')\n"
+        "for name, c in g['cases'].items():\n"
+        "    outs = mg.run_reference(ref, *[c['inputs'][k] for k in ['x','w_up','b_up','w_down','b_down','offs','grad_out']])\n"
+        "    for k, v in outs.items():\n"
+        "        w = c['outputs'][k]\n"
+        "        assert (v is None and w is None) or torch.equal(v.to(torch.bfloat16), w), (name, k)\n"
+        "print('OK')\n"
+    )
+    r = subprocess.run([sys.executable, "-c", child, str(repo), str(staged)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stderr[-2000:]
