@@ -66,6 +66,7 @@ def parse_args():
                          "(the extra GEMM's FLOPs are not counted in the metric)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-baseline-only", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--no-extra", action="store_true",
                     help="N=1: skip the secondary measurements (cfg2 forward, cfg5 at 4096 tokens, cfg4 at N=1)")
     ap.add_argument("--tokens", type=int, default=0,
@@ -317,20 +318,19 @@ def cpu_case(counts, H, I, seed=123):
 
 def cpu_sample_tflops(args, world, target_s=12.0):
     """cpu_baseline of this arm's line: the CPU reference on a bounded sample of the workload -- the
-    first experts of its routing, whole, up to about a quarter of the rows -- repeated until about
-    target_s seconds of CPU work were timed."""
+    first experts of its routing, whole, up to about an eighth of the rows -- one untimed run, then
+    repeated until about target_s seconds of CPU work were timed."""
     cref = CpuReference()
     counts, H, I, _ = cpu_counts(args, world)
     keep, rows = 0, 0
     for c in counts.tolist():
-        if rows >= max(1, int(counts.sum()) // 4):
+        if rows >= max(1, int(counts.sum()) // 8):
             break
         keep += 1
         rows += c
     case = cpu_case(counts[:keep], H, I)
-    t0 = time.perf_counter()
     cref.step(case)
-    reps, total = 1, time.perf_counter() - t0
+    reps, total = 0, 0.0
     while total < target_s and reps < 20:
         t0 = time.perf_counter()
         cref.step(case)
@@ -338,8 +338,26 @@ def cpu_sample_tflops(args, world, target_s=12.0):
         reps += 1
     value = 18.0 * rows * H * I * reps / total / 1e12
     sample = (f"{cref.what}: fwd+bwd of the first {keep} of {counts.numel()} experts of this workload's routing "
-              f"({rows} routed rows, H={H}, I={I}), {reps} repetitions, {total:.1f} s of CPU work")
+              f"({rows} routed rows, H={H}, I={I}), one untimed run then {reps} timed, {total:.1f} s of CPU work")
     return {"value": value, "unit": UNIT, "cores": cref.cores, "kind": cref.kind, "sample": sample}
+
+
+def cpu_baseline_subprocess(args):
+    """cpu_sample_tflops in a child process: the reference layer registers the same `grouped_mm`
+    operator namespace as this repository's native library, so it cannot share this process."""
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--cpu-baseline-only", "--workload", args.workload]
+    if args.tokens:
+        cmd += ["--tokens", str(args.tokens)]
+    if args.experts:
+        cmd += ["--experts", str(args.experts)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=dict(os.environ, **MALLOC_ENV))
+        lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if r.returncode == 0 and lines:
+            return json.loads(lines[-1])
+        return {"error": f"rc={r.returncode}: {r.stderr[-300:]}"}
+    except Exception as e:
+        return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 
 
 def reference_arm(args, rank, world):
@@ -597,14 +615,15 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.cpu_baseline_only:
+        print(json.dumps(cpu_sample_tflops(args, 1)), flush=True)
+        return
     if args.impl == "reference":
         if rank != 0:
             return
         _reexec_with_malloc_env()
         reference_arm(args, rank, world)
         return
-    if world == 1 and not args.no_cpu_baseline:
-        _reexec_with_malloc_env()
 
     import torch
     import torch.distributed as dist
@@ -738,7 +757,7 @@ def main():
         line["extra"] = extra_workloads(args, mgf, device, peaks, peak_src)
 
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample_tflops(args, world)
+        line["cpu_baseline"] = cpu_baseline_subprocess(args)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

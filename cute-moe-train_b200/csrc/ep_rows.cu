@@ -94,12 +94,40 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) combine_rows_kernel(
 // Rows written straight into other GPUs' memory (NVLink peer stores through CUDA IPC mappings):
 // dst_rank[i]'s buffer (peer_bases[dst_rank[i]]) row dst_row[i] = scale[i] * src[src_idx[i]].
 // The row count is n_max, or *n_dev when given (a device-side count, never read by the host).
+//
+// Completion signal (sig.flag_bases != nullptr): every block fences its stores system-wide and
+// counts itself on sig.counter; the last block of the launch then writes sig.seq into slot
+// sig.rank of every rank's flag array (a release store over NVLink) and resets the counter for the
+// next launch.  A reader waits for seq in all slots of its own flag array (wait_flags_kernel):
+// then every source's rows have landed.  This replaces a collective barrier between the pushes
+// and the kernels that read them.
+struct PushSignal {
+  const unsigned long long* flag_bases;  // device [world]: address of each rank's flag array
+  unsigned long long* counter;           // device: blocks of this launch that finished (starts at 0)
+  unsigned long long seq;
+  int64_t rank;
+};
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
     const __nv_bfloat16* __restrict__ src, int64_t ld_src, const int64_t* __restrict__ src_idx,
     const float* __restrict__ scale, int64_t n_max, const int32_t* __restrict__ n_dev,
     const int64_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
     const unsigned long long* __restrict__ peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
-    int64_t row_vec, int64_t n_src, unsigned int* __restrict__ status) {
+    int64_t row_vec, int64_t n_src, unsigned int* __restrict__ status, PushSignal sig) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -131,8 +159,39 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
       }
     }
   }
-  // make the peer stores visible system-wide before the stream's next (barrier) operation
+  // make the peer stores visible system-wide before the signal (or the stream's next operation)
   __threadfence_system();
+  if (sig.flag_bases == nullptr) return;
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(sig.counter, 1ull) == static_cast<unsigned long long>(gridDim.x) - 1ull;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();  // every block's stores (fenced before its count) precede the flags
+  for (int64_t r = threadIdx.x; r < world; r += blockDim.x) {
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(sig.flag_bases[r]);
+    st_release_sys_u64(flags + sig.rank, sig.seq);
+  }
+  if (threadIdx.x == 0) *sig.counter = 0ull;  // the next launch is stream-ordered after this one
+}
+
+// Wait until every slot s < world of this rank's flag array holds a value >= seq (all sources
+// finished the push with that sequence number), at most timeout_ns; on time-out record
+// MGF_DEV_WAIT_TIMEOUT and return (the kernels that follow then read incomplete data, which the
+// status check reports).  One block; thread s polls slot s.
+__global__ void wait_flags_kernel(const unsigned long long* __restrict__ flags, int64_t world, unsigned long long seq,
+                                  int64_t timeout_ns, unsigned int* __restrict__ status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int64_t s = threadIdx.x; s < world; s += blockDim.x) {
+    uint32_t it = 0;
+    while (ld_acquire_sys_u64(flags + s) < seq) {
+      if ((++it & 63u) == 0 && globaltimer_ns() - t0 > static_cast<uint64_t>(timeout_ns)) {
+        atomicOr(status, MGF_DEV_WAIT_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 int grid_for(int64_t rows) {
@@ -187,12 +246,16 @@ extern "C" int mgf_combine_rows(const void* rows, int64_t ld_rows, int64_t n_row
 }
 
 extern "C" int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* src_idx,
-                             const float* scale, int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
-                             const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
-                             int64_t row_elems, void* stream) {
+                             const float* scale, int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank,
+                             const int64_t* dst_row, const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
+                             int64_t row_elems, const unsigned long long* flag_bases,
+                             unsigned long long* counter, unsigned long long seq, int64_t rank, void* stream) {
   using namespace mgf;
   if (n_max < 0 || row_elems < 0 || n_src < 0) return MGF_ERR_INVALID_ARGUMENT;
-  if (n_max == 0 || row_elems == 0) return MGF_OK;
+  if (flag_bases != nullptr && (counter == nullptr || rank < 0 || rank >= world)) return MGF_ERR_INVALID_ARGUMENT;
+  const PushSignal sig{flag_bases, counter, seq, rank};
+  if (n_max == 0 || row_elems == 0) n_max = 0;  // nothing to move, but a signal still goes out
+  if (n_max == 0 && flag_bases == nullptr) return MGF_OK;
   if (src == nullptr || dst_rank == nullptr || dst_row == nullptr || peer_bases == nullptr)
     return MGF_ERR_INVALID_ARGUMENT;
   if (row_elems % 8 || ld_src % 8 || ld_dst % 8 || !aligned16(src)) return MGF_ERR_ALIGNMENT;
@@ -200,7 +263,7 @@ extern "C" int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, con
   if (status == nullptr) return MGF_ERR_CUDA;
   push_rows_kernel<<<grid_for(n_max), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), ld_src, src_idx, scale, n_max, n_dev, dst_rank, dst_row, peer_bases,
-      world, dst_rows, ld_dst, row_elems / 8, n_src, status);
+      world, dst_rows, ld_dst, row_elems / 8, n_src, status, sig);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 
@@ -246,4 +309,15 @@ extern "C" int mgf_ipc_open(const void* handle, void** base_out) {
 extern "C" int mgf_ipc_close(void* base) {
   if (base == nullptr) return MGF_ERR_INVALID_ARGUMENT;
   return cudaIpcCloseMemHandle(base) == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_wait_flags(const unsigned long long* flags, int64_t world, unsigned long long seq,
+                              int64_t timeout_ns, void* stream) {
+  using namespace mgf;
+  if (flags == nullptr || world <= 0 || world > 1024 || timeout_ns <= 0) return MGF_ERR_INVALID_ARGUMENT;
+  unsigned int* status = status_word_address();
+  if (status == nullptr) return MGF_ERR_CUDA;
+  const int threads = world <= 32 ? 32 : (world <= 256 ? 256 : 1024);
+  wait_flags_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, seq, timeout_ns, status);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }

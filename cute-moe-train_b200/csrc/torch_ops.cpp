@@ -575,7 +575,9 @@ Tensor combine_rows_cuda(const Tensor& rows, const Tensor& pos_in, const std::op
 // Rows of src pushed into other ranks' IPC-mapped buffers (see mgf_push_rows).
 void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, const std::optional<Tensor>& scale,
                     const std::optional<Tensor>& n_dev, const Tensor& dst_rank, const Tensor& dst_row,
-                    const Tensor& peer_bases, int64_t dst_rows, int64_t ld_dst, int64_t n_max) {
+                    const Tensor& peer_bases, int64_t dst_rows, int64_t ld_dst, int64_t n_max,
+                    const std::optional<Tensor>& flag_bases, const std::optional<Tensor>& counter, int64_t seq,
+                    int64_t rank) {
   check_rows(src, "src");
   const c10::cuda::CUDAGuard guard(src.device());
   TORCH_CHECK(dst_rank.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong &&
@@ -600,12 +602,33 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
     TORCH_CHECK(n_dev->scalar_type() == at::kInt && n_dev->numel() >= 1, "push_rows: n_dev must be int32");
     nd = n_dev->data_ptr<int32_t>();
   }
-  check_launch(mgf_push_rows(src.data_ptr(), src.stride(0), src.size(0), si, sc, n_max, nd, dst_rank.data_ptr<int64_t>(),
-                             dst_row.data_ptr<int64_t>(),
+  const unsigned long long* fb = nullptr;
+  unsigned long long* ctr = nullptr;
+  if (flag_bases.has_value()) {
+    TORCH_CHECK(counter.has_value() && flag_bases->scalar_type() == at::kLong && flag_bases->is_contiguous() &&
+                    flag_bases->numel() == peer_bases.numel() && counter->scalar_type() == at::kLong &&
+                    counter->numel() >= 1,
+                "push_rows: flag_bases must be int64 [world] and counter an int64 device word");
+    fb = reinterpret_cast<const unsigned long long*>(flag_bases->data_ptr<int64_t>());
+    ctr = reinterpret_cast<unsigned long long*>(counter->data_ptr<int64_t>());
+  }
+  check_launch(mgf_push_rows(src.data_ptr(), src.stride(0), src.size(0), si, sc, n_max, nd,
+                             dst_rank.data_ptr<int64_t>(), dst_row.data_ptr<int64_t>(),
                              reinterpret_cast<const unsigned long long*>(peer_bases.data_ptr<int64_t>()),
-                             peer_bases.numel(), dst_rows, ld_dst, src.size(1),
-                             at::cuda::getCurrentCUDAStream().stream()),
+                             peer_bases.numel(), dst_rows, ld_dst, src.size(1), fb, ctr,
+                             static_cast<unsigned long long>(seq), rank, at::cuda::getCurrentCUDAStream().stream()),
                "push_rows");
+}
+
+// Wait on the current stream until every slot of this rank's flag array reaches seq (see mgf_wait_flags).
+void wait_flags_cuda(const Tensor& flags, int64_t seq, int64_t timeout_ns) {
+  TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kLong && flags.is_contiguous(),
+              "wait_flags: flags must be a contiguous int64 CUDA tensor");
+  const c10::cuda::CUDAGuard guard(flags.device());
+  check_launch(mgf_wait_flags(reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()), flags.numel(),
+                              static_cast<unsigned long long>(seq), timeout_ns,
+                              at::cuda::getCurrentCUDAStream().stream()),
+               "wait_flags");
 }
 
 }  // namespace
@@ -639,7 +662,9 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
   m.def(
       "push_rows(Tensor src, Tensor? src_idx, Tensor? scale, Tensor? n_dev, Tensor dst_rank, Tensor dst_row,"
-      " Tensor peer_bases, int dst_rows, int ld_dst, int n_max) -> ()");
+      " Tensor peer_bases, int dst_rows, int ld_dst, int n_max, Tensor? flag_bases=None, Tensor? counter=None,"
+      " int seq=0, int rank=0) -> ()");
+  m.def("wait_flags(Tensor flags, int seq, int timeout_ns) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
@@ -655,6 +680,7 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("gather_rows", &gather_rows_cuda);
   m.impl("combine_rows", &combine_rows_cuda);
   m.impl("push_rows", &push_rows_cuda);
+  m.impl("wait_flags", &wait_flags_cuda);
   m.impl("mm_downproj",
          [](const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
             const Tensor& aux, double alpha, double limit) {

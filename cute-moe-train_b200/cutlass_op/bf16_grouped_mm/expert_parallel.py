@@ -21,7 +21,8 @@ Two transports carry the rows.  ``ep_moe_ffn`` (above; CPU/gloo and ``transport=
 all-to-alls with host-side split sizes.  ``ep_moe_ffn_peer`` (CUDA, the default of ``EPMoEFFN``) has
 each source rank write its rows straight into the owners' receive buffers through CUDA IPC mappings
 (``grouped_mm::push_rows``: plain peer stores, no TMA, no multicast), with the whole plan computed on
-the device and one-element all-reduces as stream-ordered barriers.  No kernel reads a peer's memory.
+the device; each push signals its completion through per-rank flags in peer memory and the readers
+wait on their own flags (no collective barrier).  No kernel reads a peer's memory.
 ``expert_fn`` can replace the fused FFN (e.g. with a CPU reference for gloo tests of the routing).
 """
 
@@ -239,9 +240,12 @@ def ep_moe_ffn(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expe
 #   ret   [T*k, H]   expert outputs of this rank's token copies, sorted (forward combine target)
 #   grows [cap, H]   gradients of `rows`                                 (backward of the combine)
 #   gret  [T*k, H]   gradients of this rank's token copies               (backward of the dispatch)
-# cap = T*k*world, the most rows one rank can receive.  All destination rows are computed on the
-# device from the all-gathered (source rank, expert) count matrix, so no split size is read on the
-# host.  A stream-ordered NCCL all-reduce of one element separates the writers from the readers.
+# cap = ceil(capacity_factor * T*k) rows, the most one rank can receive (rows past it are skipped
+# and reported through the device status word, MGF_DEV_ROW_OUT_OF_RANGE).  All destination rows
+# are computed on the device from the all-gathered (source rank, expert) count matrix, so no split
+# size is read on the host.  Each push signals its completion through the ranks' flag arrays and
+# the readers wait on their own flags; the count all-gather at the start of a call orders it after
+# every rank's use of the buffers in the previous call.
 
 
 def push_plan(c_all: torch.Tensor, e_sorted: torch.Tensor, rank: int, world: int, e_local: int, cap: int) -> dict:
@@ -280,16 +284,29 @@ def push_plan(c_all: torch.Tensor, e_sorted: torch.Tensor, rank: int, world: int
 
 
 class PeerBuffers:
-    """Receive buffers shared with every rank of `group` through CUDA IPC (allocated once)."""
+    """Receive buffers shared with every rank of `group` through CUDA IPC (allocated once), plus the
+    completion flags of the pushes.
+
+    Each rank owns a uint64 flag array [world], IPC-shared like the buffers: a push launch with
+    sequence number q writes q into slot `rank` of every rank's flags once all of its rows are
+    visible (mgf_push_rows' completion signal), and a reader waits on its own array until every slot
+    holds q (mgf_wait_flags).  Every rank issues the same pushes in the same order, so the sequence
+    numbers agree without any exchange."""
+
+    WAIT_TIMEOUT_NS = int(float(__import__("os").environ.get("MGF_EP_WAIT_TIMEOUT_S", "5")) * 1e9)
 
     def __init__(self, shapes: dict, dtype, device, group=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.local = {k: torch.empty(v, dtype=dtype, device=device) for k, v in shapes.items()}
+        self.flags = torch.zeros(self.world, dtype=torch.int64, device=device)
+        self.counters = torch.zeros(4, dtype=torch.int64, device=device)  # one per push kind
+        self.seq = 0
         from ._ext import ipc_handle
 
-        handles = {k: ipc_handle(t.data_ptr()) for k, t in self.local.items()}
+        shared = dict(self.local, flags=self.flags)
+        handles = {k: ipc_handle(t.data_ptr()) for k, t in shared.items()}
         everyone = [None] * self.world
         dist.all_gather_object(everyone, handles, group=group)
         # Open every peer allocation with THIS rank's device current (mgf_ipc_open), so this device
@@ -299,7 +316,7 @@ class PeerBuffers:
 
         self._opened = {}
         self.bases = {}
-        for k, t in self.local.items():
+        for k, t in shared.items():
             ptrs = []
             for r in range(self.world):
                 if r == self.rank:
@@ -310,8 +327,9 @@ class PeerBuffers:
                     self._opened[handle] = ipc_open(handle)
                 ptrs.append(self._opened[handle] + offset)
             self.bases[k] = torch.tensor(ptrs, dtype=torch.int64, device=device)
-        self._flag = torch.zeros(1, dtype=torch.float32, device=device)
         self.side_stream = torch.cuda.Stream(device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are mapped (and zero) before the first signal
 
     def close(self):
         from ._ext import ipc_close
@@ -321,10 +339,15 @@ class PeerBuffers:
             ipc_close(base)
         self._opened = {}
 
-    def barrier(self):
-        """Stream-ordered: work queued after it starts only once every rank's earlier work is done."""
-        with timed("ep_peer_barrier"):
-            dist.all_reduce(self._flag, group=self.group)
+    def push(self, kind: int, src, src_idx, scale, n_dev, dst_rank, dst_row, target: str, dst_rows: int, n_max: int):
+        """One push into every rank's `target` buffer followed, on the same stream, by the wait for all
+        ranks' pushes of this round: afterwards this rank's own `target`-side data is complete."""
+        self.seq += 1
+        torch.ops.grouped_mm.push_rows(src, src_idx, scale, n_dev, dst_rank, dst_row, self.bases[target], dst_rows,
+                                       src.shape[1], n_max, self.bases["flags"], self.counters[kind:kind + 1],
+                                       self.seq, self.rank)
+        with timed("ep_peer_wait"):
+            torch.ops.grouped_mm.wait_flags(self.flags, self.seq, self.WAIT_TIMEOUT_NS)
 
 
 class _PeerState:
@@ -338,21 +361,19 @@ class _PeerDispatch(torch.autograd.Function):
     def forward(ctx, x, st):
         ctx.st = st
         with timed("ep_peer_dispatch"):
-            torch.ops.grouped_mm.push_rows(x.contiguous(), st.copy_token, None, None, st.plan["dst_rank"],
-                                           st.plan["dst_row"], st.bufs.bases["rows"], st.cap, x.shape[1], st.n)
-        st.bufs.barrier()
+            st.bufs.push(0, x.contiguous(), st.copy_token, None, None, st.plan["dst_rank"], st.plan["dst_row"],
+                         "rows", st.cap, st.n)
         return st.bufs.local["rows"].view(st.cap, x.shape[1])
 
     @staticmethod
     def backward(ctx, g_rows):
         st = ctx.st
         if getattr(st, "dispatch_bwd_done", None) is not None:
-            # already pushed (and the barrier passed) on the side stream by the expert FFN's backward
+            # already pushed (and every rank's push awaited) on the side stream by the FFN's backward
             torch.cuda.current_stream().wait_event(st.dispatch_bwd_done)
             st.dispatch_bwd_done = None
         else:
             _push_rows_grad(g_rows, st)
-            st.bufs.barrier()
         with timed("ep_combine"):
             gx = torch.ops.grouped_mm.combine_rows(st.bufs.local["gret"], st.inv_order, None, st.k)
         return gx, None
@@ -361,20 +382,19 @@ class _PeerDispatch(torch.autograd.Function):
 def _push_rows_grad(g_rows: torch.Tensor, st) -> None:
     """Gradient of the dispatch: each received row's gradient goes back to its source's `gret`."""
     with timed("ep_peer_dispatch_bwd"):
-        torch.ops.grouped_mm.push_rows(g_rows.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
-                                       st.plan["src_pos"], st.bufs.bases["gret"], st.n, g_rows.shape[1], st.cap)
+        st.bufs.push(3, g_rows.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"], st.plan["src_pos"],
+                     "gret", st.n, st.cap)
 
 
 def _start_dispatch_bwd(g_rows: torch.Tensor, st) -> None:
-    """Push the rows' gradient and pass the barrier on the side stream, so both run under the
-    up-projection weight gradient that the expert FFN's backward launches next; the dispatch's
+    """Push the rows' gradient and wait for every rank's push on the side stream, so both run under
+    the up-projection weight gradient that the expert FFN's backward launches next; the dispatch's
     backward then only waits for the recorded event."""
     side = st.side_stream
     side.wait_stream(torch.cuda.current_stream())
     g_rows.record_stream(side)
     with torch.cuda.stream(side):
         _push_rows_grad(g_rows, st)
-        st.bufs.barrier()
         ev = torch.cuda.Event()
         ev.record(side)
     st.dispatch_bwd_done = ev
@@ -385,7 +405,7 @@ class _EPExpertFFN(torch.autograd.Function):
 
     Same launches and results as the two wrappers; the backward hands the received rows' gradient
     to the dispatch push on a side stream as soon as the up-projection dgrad has produced it, before
-    launching the up-projection weight gradient, so the NVLink push and its barrier overlap that GEMM
+    launching the up-projection weight gradient, so the NVLink push and its wait overlap that GEMM
     (the push kernel's blocks co-reside with the GEMM's one CTA per SM).
     """
 
@@ -424,9 +444,8 @@ class _PeerCombine(torch.autograd.Function):
         ctx.st, ctx.has_w = st, w_flat is not None
         ctx.save_for_backward(w_flat if w_flat is not None else y.new_empty(0))
         with timed("ep_peer_combine"):
-            torch.ops.grouped_mm.push_rows(y.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"],
-                                           st.plan["src_pos"], st.bufs.bases["ret"], st.n, y.shape[1], st.cap)
-        st.bufs.barrier()
+            st.bufs.push(1, y.contiguous(), None, None, st.plan["n_recv"], st.plan["src_rank"], st.plan["src_pos"],
+                         "ret", st.n, st.cap)
         with timed("ep_combine"):
             return torch.ops.grouped_mm.combine_rows(st.bufs.local["ret"], st.inv_order, w_flat, st.k)
 
@@ -437,9 +456,8 @@ class _PeerCombine(torch.autograd.Function):
         g = g.contiguous()
         scale = w_flat[st.order].contiguous() if ctx.has_w else None
         with timed("ep_peer_combine_bwd"):
-            torch.ops.grouped_mm.push_rows(g, st.copy_token, scale, None, st.plan["dst_rank"], st.plan["dst_row"],
-                                           st.bufs.bases["grows"], st.cap, g.shape[1], st.n)
-        st.bufs.barrier()
+            st.bufs.push(2, g, st.copy_token, scale, None, st.plan["dst_rank"], st.plan["dst_row"], "grows", st.cap,
+                         st.n)
         grad_w = None
         if ctx.has_w and ctx.needs_input_grad[1]:
             copies = st.bufs.local["ret"][st.inv_order].float().view(-1, st.k, g.shape[1])
@@ -449,11 +467,14 @@ class _PeerCombine(torch.autograd.Function):
 
 def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
                     bufs_cache: dict, group=None, router_weights: torch.Tensor | None = None,
-                    overlap: bool = False) -> tuple:
+                    overlap: bool = False, capacity_factor: float = 2.0) -> tuple:
     """Expert-parallel MoE FFN with dispatch/combine as peer-memory pushes (CUDA, world > 1).
 
-    Same contract as ep_moe_ffn.  Every rank must pass the same number of tokens.  The receive buffers
-    of one call stay live until its backward ran; a second forward before that backward raises.
+    Same contract as ep_moe_ffn.  Every rank must pass the same number of tokens.  Each rank can
+    receive at most ceil(capacity_factor * T * k) token copies (at most T * k * world); copies past
+    that are dropped and MGF_DEV_ROW_OUT_OF_RANGE / MGF_DEV_BAD_OFFS are recorded in the device status
+    word, which check_device_status() turns into a RuntimeError.  The receive buffers of one call stay
+    live until its backward ran; a second forward before that backward raises.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -462,8 +483,10 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
     T, H = x.shape
     k = expert_idx.shape[1]
     e_local = num_experts // world
-    n, cap = T * k, T * k * world
-    key = (n, H, x.dtype)
+    n = T * k
+    cap = min(n * world, int(math.ceil(capacity_factor * n)))
+    cap = (cap + 7) // 8 * 8
+    key = (n, cap, H, x.dtype)
     bufs = bufs_cache.get(key)
     if bufs is None:
         bufs = PeerBuffers({"rows": (cap, H), "grows": (cap, H), "ret": (n, H), "gret": (n, H)}, x.dtype, x.device,
@@ -504,12 +527,15 @@ class EPMoEFFN(torch.nn.Module):
 
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
                  swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer",
-                 overlap: bool = False):
+                 overlap: bool = False, capacity_factor: float = 2.0):
         """transport: "peer" (NVLink pushes, CUDA, world > 1) or "nccl" (all-to-all).  overlap (peer
         transport): push the dispatch's gradient on a side stream under the up-projection weight
-        gradient instead of after it."""
+        gradient instead of after it.  capacity_factor (peer transport): receive buffers hold
+        ceil(capacity_factor * tokens * topk) rows per rank (overflow is reported, see
+        ep_moe_ffn_peer)."""
         super().__init__()
         self.overlap = overlap
+        self.capacity_factor = capacity_factor
         if transport not in ("peer", "nccl"):
             raise ValueError(f"transport must be 'peer' or 'nccl', got {transport!r}")
         self.transport = transport
@@ -547,7 +573,8 @@ class EPMoEFFN(torch.nn.Module):
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if self.transport == "peer" and world > 1 and x.is_cuda:
             out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self._peer_expert_fn, self._peer_bufs,
-                                      self.group, router_weights, overlap=self.overlap)
+                                      self.group, router_weights, overlap=self.overlap,
+                                      capacity_factor=self.capacity_factor)
             self.last_local_rows = st.plan["n_recv"]  # device tensor; read it outside timed regions
             return out
         out, plan = ep_moe_ffn(x, expert_idx, self.num_experts, self.expert_fn, self.group, router_weights)

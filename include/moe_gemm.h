@@ -160,12 +160,24 @@ int mgf_combine_rows(const void* rows, int64_t ld_rows, int64_t n_rows, const in
  * peer_bases[dst_rank[i]] (device array of `world` base addresses, one per rank, from CUDA IPC
  * mappings; each buffer dst_rows rows of stride ld_dst).  Rows whose rank or destination row falls
  * outside [0, world) x [0, dst_rows), or whose source row falls outside [0, n_src), are skipped and
- * set MGF_DEV_ROW_OUT_OF_RANGE.  Plain peer stores, no multicast; the caller orders them before
- * the readers with a stream-ordered barrier. */
+ * set MGF_DEV_ROW_OUT_OF_RANGE.  Plain peer stores, no multicast.
+ * Completion signal (flag_bases non-NULL): when all of the launch's stores are visible, `seq` is
+ * written (release, system scope) into slot `rank` of every rank's flag array (flag_bases: device
+ * array of `world` addresses of uint64 [world] flag arrays, IPC-mapped); `counter` is a zeroed
+ * device uint64 of this rank that the launch uses and leaves at zero.  Readers then call
+ * mgf_wait_flags on their own flag array instead of a collective barrier. */
 int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* src_idx, const float* scale,
                   int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
                   const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
-                  int64_t row_elems, void* stream);
+                  int64_t row_elems, const unsigned long long* flag_bases, unsigned long long* counter,
+                  unsigned long long seq, int64_t rank, void* stream);
+
+/* Wait on `stream` until flags[s] >= seq for every s < world (every rank's push with sequence
+ * number seq has landed here), at most timeout_ns; a wait that runs out records
+ * MGF_DEV_WAIT_TIMEOUT in the device status word and returns.  One small kernel, no host sync
+ * (no counterpart in the reference). */
+int mgf_wait_flags(const unsigned long long* flags, int64_t world, unsigned long long seq, int64_t timeout_ns,
+                   void* stream);
 
 /* Map a peer process's device allocation (its 64-byte cudaIpcMemHandle_t) into the context of
  * the calling thread's current device, peer access enabled, for mgf_push_rows destinations

@@ -232,3 +232,69 @@ def test_ep_world2_every_transport_matches_oracle():
             _check_ep(transport, [torch.from_numpy(a) for a in res[rank][transport]], want, rank, E // 2)
         for a, b in zip(res[rank]["peer_overlap"], res[rank]["peer"]):
             assert (a == b).all(), f"rank{rank}: overlap changed the result"
+
+
+def _overflow_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        from conftest import PKG  # noqa: F401
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+        try:
+            from cutlass_op.bf16_grouped_mm import _ext
+            from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
+
+            _ext.device_status(clear=True)
+            ffn = EPMoEFFN(E, H, I, device=dev, seed=5, capacity_factor=0.25)  # far below the ~1x received
+            x = torch.randn(T, H, generator=torch.Generator().manual_seed(10 + rank)).to(torch.bfloat16)
+            x = x.to(dev).requires_grad_(True)
+            idx = route_tokens(T, E, K, "zipf", seed=20 + rank).to(dev)
+            out = ffn(x, idx)
+            out.float().sum().backward()
+            torch.cuda.synchronize()
+            st = _ext.device_status(clear=False)
+            try:
+                _ext.check_device_status()
+                raised = False
+            except RuntimeError:
+                raised = True
+            q.put((rank, {"status": st, "raised": raised, "after": _ext.device_status(clear=True)}))
+        finally:
+            dist.destroy_process_group()
+    except Exception:
+        import traceback
+
+        q.put((rank, "error", traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_world2_capacity_overflow_is_reported():
+    """Receive buffers far below the rows a rank receives: the pushes skip the rows past the
+    capacity, nothing outside the buffers is touched, and the device status word reports it on the
+    host (check_device_status raises RuntimeError)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_overflow_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=300)
+            assert not (isinstance(r[1], str) and r[1] == "error"), r[2]
+            res[r[0]] = r[1]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank in range(2):
+        assert res[rank]["status"] & 0x4, res[rank]        # MGF_DEV_ROW_OUT_OF_RANGE
+        assert res[rank]["raised"] and res[rank]["after"] == 0, res[rank]

@@ -231,7 +231,7 @@ def test_rows_past_offs_end_are_never_written():
     s_out = torch.full((M, I), nan, dtype=torch.bfloat16, device="cuda")
     aux_out = torch.full((M, 2 * I), nan, dtype=torch.bfloat16, device="cuda")
     _ext._grouped_mm_swiglu_cuda(xp, w_up, offs, b_up, aux_out, s_out, 1.702, 7.0, True)
-    g_packed = torch.full((M, I), nan, dtype=torch.float32, device="cuda")
+    g_packed = torch.full((M, 2 * I), nan, dtype=torch.bfloat16, device="cuda").view(torch.float32)
     _ext._grouped_mm_swiglu_bwd_cuda(gp, w_down.transpose(-2, -1), offs, aux_out.view(torch.float32), g_packed,
                                      1.702, 7.0)
     torch.cuda.synchronize()
