@@ -55,6 +55,9 @@ def parse_args():
                     help="expert-parallel routing (cfg4 lists both; uniform is the balanced case)")
     ap.add_argument("--ep-overlap", action="store_true",
                     help="peer transport: push the dispatch gradient under the up-proj weight gradient")
+    ap.add_argument("--ep-unfused", action="store_true",
+                    help="peer transport: separate push kernels for the combine and the dispatch gradient instead "
+                         "of the GEMM scatter epilogues")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
@@ -175,7 +178,9 @@ def build_workload(args, rank, world, device):
     E_total = args.experts or 128
     desc = (f"cfg4: GPT-OSS-120B experts E={E_total} H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
             f"expert parallel E/{world} per GPU, dispatch/combine by "
-            + ("peer-memory pushes over NVLink" if args.transport == "peer" else "NCCL all-to-all")
+            + (("peer-memory pushes over NVLink" + ("" if args.ep_unfused else
+                                                     ", combine and dispatch gradient stored by the GEMM epilogues"))
+               if args.transport == "peer" else "NCCL all-to-all")
             + (", dispatch gradient pushed under the up-proj wgrad" if args.ep_overlap else ""))
     return wl, desc, E_total, 0, tokens, topk, H, I, 1.1, False
 
@@ -444,7 +449,8 @@ def ep_parity_check(args, world, rank, device):
     from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
     T, E, H, I, K = 512, 8 * world, 256, 128, 4
-    ffn = EPMoEFFN(E, H, I, device=device, seed=77, transport=args.transport, overlap=args.ep_overlap)
+    ffn = EPMoEFFN(E, H, I, device=device, seed=77, transport=args.transport, overlap=args.ep_overlap,
+                   fused=not args.ep_unfused)
     g = torch.Generator().manual_seed(500 + rank)
     x = torch.randn(T, H, generator=g).to(torch.bfloat16)
     w = torch.rand(T, K, generator=g)
@@ -667,7 +673,7 @@ def main():
         ep_parity = ep_parity_check(args, world, rank, device)
         torch.cuda.empty_cache()
         ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport,
-                       overlap=args.ep_overlap)
+                       overlap=args.ep_overlap, fused=not args.ep_unfused)
         gx = torch.Generator(device=device).manual_seed(1 + rank)
         x = torch.randn(tokens, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
         expert_idx = route_tokens(tokens, E_total, topk, args.routing, seed=100 + rank, device=device)
@@ -767,37 +773,43 @@ def main():
 def compare_torch(step_inputs, steps, warmup, flops, fwd_only=False):
     """torch._grouped_mm + eager bias / clamped SwiGLU / autograd on the same inputs and GPU.
 
-    The per-expert biases are added in place, one row block per expert (no [M, N] gathered bias
-    tensor).  Besides the whole step it times the same graph without the bias and SwiGLU (the two
-    torch._grouped_mm GEMMs and their autograd alone), so the line shows how the step splits into
-    grouped-GEMM time and eager-op time."""
+    Three forms of the same step are timed:
+      * ``ms_per_step`` (the comparator): per-row biases gathered as b[row_expert] and added
+        (one [M, N] gather per bias; the fastest eager form measured here);
+      * ``inplace_bias_ms``: the biases added in place, one row block per expert (no gathered
+        tensor, but E small kernels and their autograd copies);
+      * ``grouped_mm_only_ms``: the graph without bias and SwiGLU -- the two torch._grouped_mm GEMMs
+        and their autograd alone (same FLOPs), so ``eager_ops_ms`` = comparator - this is the time
+        of the unfused eager operations."""
     import torch
 
     x, w_up, b_up, w_down, b_down, offs, counts = step_inputs
     try:
         bounds = torch.cumsum(counts.cpu(), 0).tolist()
         starts = [0] + bounds[:-1]
+        row_e = torch.repeat_interleave(torch.arange(len(counts), device=x.device), counts.to(x.device))
         xs = x.detach().clone().requires_grad_(True)
         wu, bu, wd, bd = [t.detach().clone().requires_grad_(True) for t in (w_up, b_up, w_down, b_down)]
         params = [xs, wu, bu, wd, bd]
         ones = torch.ones(x.shape[0], w_down.shape[-1], dtype=x.dtype, device=x.device)
 
-        def add_bias(h, b):
-            # in place on each expert's row block (torch._grouped_mm's backward does not need its output)
-            for e, (s0, s1) in enumerate(zip(starts, bounds)):
+        def add_bias(h, b, mode):
+            if mode == "gather":
+                return h + b[row_e]
+            for e, (s0, s1) in enumerate(zip(starts, bounds)):  # in place on each expert's row block
                 if s1 > s0:
                     h[s0:s1] += b[e]
             return h
 
-        def make(eager: bool):
+        def make(mode):
             def step():
                 for p in params:
                     p.grad = None
                 ctx = torch.no_grad() if fwd_only else torch.enable_grad()
                 with ctx:
                     h = torch._grouped_mm(xs, wu, offs=offs)
-                    if eager:
-                        h = add_bias(h, bu)
+                    if mode != "gemm_only":
+                        h = add_bias(h, bu, mode)
                         g = h[:, 0::2].clamp(max=LIMIT)
                         u = h[:, 1::2].clamp(min=-LIMIT, max=LIMIT)
                         s_ = g * torch.sigmoid(ALPHA * g) * (u + 1.0)
@@ -806,20 +818,22 @@ def compare_torch(step_inputs, steps, warmup, flops, fwd_only=False):
                     if fwd_only:
                         return
                     out = torch._grouped_mm(s_, wd, offs=offs)
-                    if eager:
-                        out = add_bias(out, bd)
+                    if mode != "gemm_only":
+                        out = add_bias(out, bd, mode)
                     # d(out.sum())/d(out) as a materialised tensor: torch._grouped_mm's backward rejects the
                     # zero-stride expanded gradient that out.sum().backward() produces.
                     out.backward(ones)
             return step
 
-        ms = time_steps(make(True), steps, warmup)
-        ms_gemm = time_steps(make(False), max(3, steps // 2), warmup)
+        ms = time_steps(make("gather"), steps, warmup)
+        short = max(3, steps // 3)
+        ms_inplace = time_steps(make("inplace"), short, min(warmup, 3))
+        ms_gemm = time_steps(make("gemm_only"), short, min(warmup, 3))
         return {"ms_per_step": ms, "value": flops / (ms * 1e-3) / 1e12, "unit": UNIT,
-                "grouped_mm_only_ms": ms_gemm, "eager_ops_ms": ms - ms_gemm,
-                "what": "torch._grouped_mm + eager per-expert bias / clamped SwiGLU / autograd, same inputs, same "
-                        "GPU; grouped_mm_only_ms = the same graph without bias and SwiGLU (the two grouped GEMMs "
-                        "and their autograd), eager_ops_ms = the difference"}
+                "inplace_bias_ms": ms_inplace, "grouped_mm_only_ms": ms_gemm, "eager_ops_ms": ms - ms_gemm,
+                "what": "torch._grouped_mm + eager gathered per-row bias / clamped SwiGLU / autograd, same inputs, "
+                        "same GPU; inplace_bias_ms = biases added in place per expert block; grouped_mm_only_ms = the "
+                        "two grouped GEMMs and their autograd without bias and SwiGLU; eager_ops_ms = the difference"}
     except Exception as e:  # report, do not fail the bench
         return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 

@@ -321,3 +321,249 @@ extern "C" int mgf_wait_flags(const unsigned long long* flags, int64_t world, un
   wait_flags_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, seq, timeout_ns, status);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
+
+// ============================================================================ expert-parallel plan
+//
+// The device-side plan of the peer transport, three launches and no host synchronisation:
+//   ep_sort      a stable counting sort of this rank's T*k routed copies by expert id (one block):
+//                order / inverse / token of every sorted copy, and the per-expert counts that the
+//                caller all-gathers into c_all [world, E];
+//   ep_tables    prefix sums of c_all (one block) into a small int32 workspace;
+//   ep_routes    elementwise: for sorted copy p its owner rank and row in the owner's receive
+//                buffer; for row j of this rank's receive buffer its source rank and sorted
+//                position there, the row's addresses in the sources' `ret` / `gret` buffers (for
+//                the scatter epilogues), the int32 offs of the local experts and the row count.
+// Owner row layout: local expert-major, then source rank, then the source's copies in sorted order.
+
+namespace mgf {
+namespace {
+
+__global__ void __launch_bounds__(1024) ep_sort_kernel(const int64_t* __restrict__ ids, int64_t n, int E, int k,
+                                                      int64_t* __restrict__ order, int64_t* __restrict__ inv,
+                                                      int64_t* __restrict__ token, int64_t* __restrict__ e_sorted,
+                                                      int64_t* __restrict__ counts, unsigned int* __restrict__ status) {
+  extern __shared__ int sh[];  // hist[32][E], tot[E]
+  int* tot = sh + 32 * E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t chunk = (n + 31) / 32;
+  const int64_t lo = warp * chunk;
+  const int64_t hi = lo + chunk < n ? lo + chunk : n;
+  int* h = sh + warp * E;
+  for (int e = lane; e < E; e += 32) h[e] = 0;
+  __syncwarp();
+  bool bad = false;
+  for (int64_t i = lo + lane; i < hi; i += 32) {
+    int64_t e = __ldg(ids + i);
+    if (e < 0 || e >= E) {
+      bad = true;
+      e = e < 0 ? 0 : E - 1;
+    }
+    atomicAdd(&h[e], 1);
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {  // exclusive prefix over warps, per expert
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = sh[w * E + e];
+      sh[w * E + e] = run;
+      run += c;
+    }
+    tot[e] = run;
+    counts[e] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive prefix of the totals over experts (in place)
+    int carry = 0;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      const int v = e < E ? tot[e] : 0;
+      int inc = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
+      }
+      if (e < E) tot[e] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 32 * E; idx += blockDim.x) sh[idx] += tot[idx % E];
+  __syncthreads();
+  // in order, 32 copies at a time: rank among the same expert's lanes, then the group's last lane
+  // advances the expert's cursor
+  for (int64_t base = lo; base < hi; base += 32) {
+    const int64_t i = base + lane;
+    const bool v = i < hi;
+    int e = -1;
+    if (v) {
+      const int64_t r = __ldg(ids + i);
+      e = r < 0 ? 0 : (r >= E ? E - 1 : static_cast<int>(r));
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (v) {
+      const int pos = h[e] + __popc(peers & ((1u << lane) - 1u));
+      order[pos] = i;
+      inv[i] = pos;
+      token[pos] = i / k;
+      e_sorted[pos] = e;
+    }
+    __syncwarp();
+    if (v && lane == 31 - __clz(peers)) h[e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// Workspace (int32) layout written by ep_tables_kernel, read by ep_routes_kernel.
+struct RouteTables {
+  int E, world, rank, e_local;
+  int* pos;      // [world][E] first sorted copy of expert e on source s (exclusive prefix over e)
+  int* dst0;     // [E] owner row of this rank's first copy of expert e: base[e] + before_rank[e]
+  int* seg_end;  // [e_local * world] inclusive prefix of this rank's (local expert, source) segments
+};
+
+__host__ __device__ inline RouteTables route_tables(int* ws, int E, int world, int rank, int e_local) {
+  RouteTables t{E, world, rank, e_local, ws, ws + world * E, ws + world * E + E};
+  return t;
+}
+
+__global__ void ep_tables_kernel(const int64_t* __restrict__ c_all, RouteTables t) {
+  const int E = t.E, world = t.world;
+  for (int s = threadIdx.x; s < world; s += blockDim.x) {  // per-source exclusive prefix over experts
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      t.pos[s * E + e] = run;
+      run += static_cast<int>(c_all[s * E + e]);
+    }
+  }
+  for (int o = threadIdx.x; o < world; o += blockDim.x) {  // per-owner rows of each expert
+    int base = 0;
+    for (int e = o * t.e_local; e < (o + 1) * t.e_local; ++e) {
+      int tot = 0, before = 0;
+      for (int s = 0; s < world; ++s) {
+        const int c = static_cast<int>(c_all[s * E + e]);
+        if (s < t.rank) before += c;
+        tot += c;
+      }
+      t.dst0[e] = base + before;
+      base += tot;
+    }
+  }
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int el = 0; el < t.e_local; ++el)
+      for (int s = 0; s < world; ++s) {
+        run += static_cast<int>(c_all[s * E + t.rank * t.e_local + el]);
+        t.seg_end[el * world + s] = run;
+      }
+  }
+}
+
+__global__ void ep_routes_kernel(const int64_t* __restrict__ e_sorted, int64_t n, int64_t cap, RouteTables t,
+                                 const unsigned long long* __restrict__ ret_bases,
+                                 const unsigned long long* __restrict__ gret_bases, int64_t row_bytes,
+                                 int64_t* __restrict__ dst_rank, int64_t* __restrict__ dst_row,
+                                 int64_t* __restrict__ src_rank, int64_t* __restrict__ src_pos,
+                                 int64_t* __restrict__ ptr_ret, int64_t* __restrict__ ptr_gret,
+                                 int32_t* __restrict__ offs, int32_t* __restrict__ n_recv) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int S = t.e_local * t.world;
+  if (i < n) {
+    const int e = static_cast<int>(e_sorted[i]);
+    dst_rank[i] = e / t.e_local;
+    dst_row[i] = t.dst0[e] + (i - t.pos[t.rank * t.E + e]);
+  }
+  if (i < cap) {
+    const int total = t.seg_end[S - 1];
+    if (i >= total) {
+      src_rank[i] = -1;
+      src_pos[i] = -1;
+      if (ptr_ret) ptr_ret[i] = 0;
+      if (ptr_gret) ptr_gret[i] = 0;
+    } else {
+      int lo = 0, hi = S - 1;  // first segment whose end is > i
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (t.seg_end[mid] > i) hi = mid; else lo = mid + 1;
+      }
+      const int el = lo / t.world, s = lo - el * t.world;
+      const int seg_start = lo == 0 ? 0 : t.seg_end[lo - 1];
+      const int64_t sp = t.pos[s * t.E + t.rank * t.e_local + el] + (i - seg_start);
+      src_rank[i] = s;
+      src_pos[i] = sp;
+      if (ptr_ret) ptr_ret[i] = static_cast<int64_t>(ret_bases[s] + sp * row_bytes);
+      if (ptr_gret) ptr_gret[i] = static_cast<int64_t>(gret_bases[s] + sp * row_bytes);
+    }
+  }
+  if (i < t.e_local) offs[i] = t.seg_end[i * t.world + t.world - 1];
+  if (i == 0) n_recv[0] = t.seg_end[S - 1];
+}
+
+__global__ void signal_flags_kernel(const unsigned long long* __restrict__ flag_bases, int64_t world, int64_t rank,
+                                    unsigned long long seq) {
+  __threadfence_system();  // the stream's earlier kernels (e.g. a scatter epilogue's peer stores) precede the flags
+  for (int64_t r = threadIdx.x; r < world; r += blockDim.x) {
+    unsigned long long* flags = reinterpret_cast<unsigned long long*>(flag_bases[r]);
+    st_release_sys_u64(flags + rank, seq);
+  }
+}
+
+}  // namespace
+}  // namespace mgf
+
+extern "C" int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk, int64_t* order,
+                           int64_t* inv_order, int64_t* copy_token, int64_t* e_sorted, int64_t* counts, void* stream) {
+  using namespace mgf;
+  if (n < 0 || n > INT32_MAX || num_experts < 1 || num_experts > 1024 || topk < 1) return MGF_ERR_INVALID_ARGUMENT;
+  if (counts == nullptr || (n > 0 && (expert_ids == nullptr || order == nullptr || inv_order == nullptr ||
+                                      copy_token == nullptr || e_sorted == nullptr)))
+    return MGF_ERR_INVALID_ARGUMENT;
+  unsigned int* status = status_word_address();
+  if (status == nullptr) return MGF_ERR_CUDA;
+  const int smem = (32 + 1) * num_experts * static_cast<int>(sizeof(int));
+  if (cudaFuncSetAttribute(ep_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return MGF_ERR_CUDA;
+  ep_sort_kernel<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(expert_ids, n, num_experts, topk, order,
+                                                                      inv_order, copy_token, e_sorted, counts,
+                                                                      status);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int64_t mgf_ep_routes_workspace_words(int32_t world, int32_t num_experts) {
+  return static_cast<int64_t>(world) * num_experts + num_experts + num_experts;
+}
+
+extern "C" int mgf_ep_routes(const int64_t* c_all, int32_t world, int32_t num_experts, const int64_t* e_sorted,
+                             int64_t n, int32_t rank, int64_t cap, const unsigned long long* ret_bases,
+                             const unsigned long long* gret_bases, int64_t row_bytes, int32_t* workspace,
+                             int64_t* dst_rank, int64_t* dst_row, int64_t* src_rank, int64_t* src_pos,
+                             int64_t* ptr_ret, int64_t* ptr_gret, int32_t* offs, int32_t* n_recv, void* stream) {
+  using namespace mgf;
+  if (world < 1 || num_experts < 1 || num_experts % world || rank < 0 || rank >= world || n < 0 || cap < 1 ||
+      n > INT32_MAX || cap > INT32_MAX || c_all == nullptr || workspace == nullptr || offs == nullptr ||
+      n_recv == nullptr || src_rank == nullptr || src_pos == nullptr ||
+      (n > 0 && (e_sorted == nullptr || dst_rank == nullptr || dst_row == nullptr)))
+    return MGF_ERR_INVALID_ARGUMENT;
+  if ((ptr_ret != nullptr && ret_bases == nullptr) || (ptr_gret != nullptr && gret_bases == nullptr))
+    return MGF_ERR_INVALID_ARGUMENT;
+  const int e_local = num_experts / world;
+  const RouteTables t = route_tables(workspace, num_experts, world, rank, e_local);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ep_tables_kernel<<<1, 32, 0, st>>>(c_all, t);
+  int64_t items = n > cap ? n : cap;
+  if (items < e_local) items = e_local;
+  const int64_t blocks = (items + 255) / 256;
+  ep_routes_kernel<<<static_cast<unsigned>(blocks > 0 ? blocks : 1), 256, 0, st>>>(
+      e_sorted, n, cap, t, ret_bases, gret_bases, row_bytes, dst_rank, dst_row, src_rank, src_pos, ptr_ret,
+      ptr_gret, offs, n_recv);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_signal_flags(const unsigned long long* flag_bases, int64_t world, int64_t rank,
+                                unsigned long long seq, void* stream) {
+  using namespace mgf;
+  if (flag_bases == nullptr || world < 1 || world > 1024 || rank < 0 || rank >= world) return MGF_ERR_INVALID_ARGUMENT;
+  signal_flags_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flag_bases, world, rank, seq);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}

@@ -104,6 +104,7 @@ struct Params {
   int d_v8, d2_v8;    // the same for the ragged-M outputs d and d2
   int stall_test;     // test hook: the producer hands out no tiles, so every consumer wait runs out
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
+  const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
 };
 
 struct TileInfo {
@@ -700,6 +701,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
         ptx::tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+        // output row of D: row `grow` of d, or (scatter mode) the address d_rows[grow] -- possibly in
+        // another GPU's memory -- with 0 meaning "no destination"; 32-byte stores only where aligned
+        __nv_bfloat16* drow = p.d + (int64_t)grow * p.ldd;
+        bool dv8 = p.d_v8;
+        if (p.d_rows != nullptr) {
+          drow = valid ? reinterpret_cast<__nv_bfloat16*>(__ldg(p.d_rows + grow)) : nullptr;
+          dv8 = p.d_v8 && (reinterpret_cast<uintptr_t>(drow) & 31u) == 0;
+        }
         if (warp_active) {
 #pragma unroll 1
           for (int c = c_begin; c < c_begin + kChunks; ++c) {
@@ -754,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint4 u[4];
 #pragma unroll
                 for (int g = 0; g < 4; ++g) u[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
-                store_units<4>(p.d + (int64_t)grow * p.ldd + col0, u, (p.n - col0) >> 3, p.d_v8);
+                if (drow != nullptr) store_units<4>(drow + col0, u, (p.n - col0) >> 3, dv8);
               }
               if constexpr (EPI == MGF_EPI_SWIGLU) {
                 uint32_t so[8];
@@ -1152,7 +1161,9 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // every group (A and B, possibly NULL, are then never read).
   if (!ragged_k && g.total_rows == 0) return MGF_OK;
   const bool no_rows = g.total_rows == 0;
-  if (g.offs == nullptr || g.d == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  const bool scatter = g.d_row_ptrs != nullptr;
+  if (scatter && (g.epilogue != MGF_EPI_BIAS || g.ab_type != MGF_AB_BF16)) return MGF_ERR_INVALID_ARGUMENT;
+  if (g.offs == nullptr || (g.d == nullptr && !scatter)) return MGF_ERR_INVALID_ARGUMENT;
   if (!no_rows && (g.a == nullptr || g.b == nullptr)) return MGF_ERR_INVALID_ARGUMENT;
 
   int dev = 0;
@@ -1189,6 +1200,8 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   };
   p.aux_v8 = v8_ok(g.aux, g.ld_aux) ? 1 : 0;
   p.d_v8 = v8_ok(g.d, g.ldd) ? 1 : 0;
+  p.d_rows = reinterpret_cast<const long long*>(g.d_row_ptrs);
+  if (scatter) p.d_v8 = (g.n % 16) == 0 ? 1 : 0;  // per-row address alignment is checked in the kernel
   p.d2_v8 = v8_ok(g.d2, g.ldd2) ? 1 : 0;
   p.alpha = g.swiglu_alpha;
   p.limit = g.swiglu_limit;
@@ -1198,7 +1211,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // TMA needs it for A and B, the epilogue's 16-byte vector stores need it for the outputs.
   auto stride_ok = [](int64_t s) { return s > 0 && (s % 8) == 0; };
   if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.d)) return MGF_ERR_ALIGNMENT;
-  if (!stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
+  if (!scatter && !stride_ok(g.ldd)) return MGF_ERR_ALIGNMENT;
   const bool f8 = g.ab_type == MGF_AB_E4M3;
   if (g.ab_type != MGF_AB_BF16 && !f8) return MGF_ERR_INVALID_ARGUMENT;
   const int esz = f8 ? 1 : 2;  // bytes per A / B element

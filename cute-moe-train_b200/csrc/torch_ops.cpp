@@ -620,6 +620,110 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
                "push_rows");
 }
 
+// Ragged-M GEMM + bias whose output rows go to per-row addresses (mgf_gemm_desc.d_row_ptrs), e.g.
+// straight into the source ranks' combine buffers.
+void mm_scatter_cuda(const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
+                     const Tensor& row_ptrs) {
+  TORCH_CHECK(a.is_cuda() && a.dim() == 2 && b.dim() == 3 && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16,
+              "mm_scatter: mat_a [rows, k] and mat_b [E, k, n] bf16 CUDA tensors");
+  TORCH_CHECK(a.stride(1) == 1, "mm_scatter: mat_a must be row-major");
+  TORCH_CHECK(offs.scalar_type() == at::kInt && offs.dim() == 1 && offs.size(0) == b.size(0),
+              "mm_scatter: offs must be int32 [E]");
+  TORCH_CHECK(row_ptrs.scalar_type() == at::kLong && row_ptrs.is_contiguous() && row_ptrs.numel() >= a.size(0),
+              "mm_scatter: row_ptrs must be contiguous int64 with one address per row");
+  if (bias.has_value()) check_bias(*bias, b.size(0), b.size(2));
+  const c10::cuda::CUDAGuard guard(a.device());
+  const bool b_col_major = check_strides_transposed(b, "mat_b");
+  mgf_gemm_desc g = base_desc();
+  g.epilogue = MGF_EPI_BIAS;
+  g.num_groups = static_cast<int32_t>(offs.numel());
+  g.total_rows = a.size(0);
+  g.k = a.size(1);
+  g.n = b.size(2);
+  g.a = a.data_ptr();
+  g.lda = a.stride(0);
+  g.b = b.data_ptr();
+  g.b_mn_major = b_col_major ? 0 : 1;
+  g.ldb = b_col_major ? b.stride(2) : b.stride(1);
+  g.ldb_batch = b.stride(0);
+  g.offs = offs.data_ptr<int32_t>();
+  if (bias.has_value()) {
+    g.bias = bias->data_ptr();
+    g.bias_stride = bias->stride(0);
+  }
+  g.d_row_ptrs = row_ptrs.data_ptr<int64_t>();
+  g.sm_carveout = sm_carveout_for(a);
+  check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), "mm_scatter");
+}
+
+void signal_flags_cuda(const Tensor& flag_bases, int64_t rank, int64_t seq) {
+  TORCH_CHECK(flag_bases.is_cuda() && flag_bases.scalar_type() == at::kLong && flag_bases.is_contiguous(),
+              "signal_flags: flag_bases must be a contiguous int64 CUDA tensor");
+  const c10::cuda::CUDAGuard guard(flag_bases.device());
+  check_launch(mgf_signal_flags(reinterpret_cast<const unsigned long long*>(flag_bases.data_ptr<int64_t>()),
+                                flag_bases.numel(), rank, static_cast<unsigned long long>(seq),
+                                at::cuda::getCurrentCUDAStream().stream()),
+               "signal_flags");
+}
+
+std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> ep_sort_cuda(const Tensor& ids_in, int64_t num_experts,
+                                                                int64_t topk) {
+  TORCH_CHECK(ids_in.is_cuda(), "ep_sort: expert ids must be a CUDA tensor");
+  const c10::cuda::CUDAGuard guard(ids_in.device());
+  Tensor ids = ids_in.reshape(-1).to(at::kLong).contiguous();
+  const int64_t n = ids.numel();
+  auto opt = ids.options();
+  Tensor order = at::empty({n}, opt), inv = at::empty({n}, opt), tok = at::empty({n}, opt),
+         es = at::empty({n}, opt), counts = at::empty({num_experts}, opt);
+  check_launch(mgf_ep_sort(ids.data_ptr<int64_t>(), n, static_cast<int32_t>(num_experts),
+                           static_cast<int32_t>(topk), order.data_ptr<int64_t>(), inv.data_ptr<int64_t>(),
+                           tok.data_ptr<int64_t>(), es.data_ptr<int64_t>(), counts.data_ptr<int64_t>(),
+                           at::cuda::getCurrentCUDAStream().stream()),
+               "ep_sort");
+  return {order, inv, tok, es, counts};
+}
+
+std::vector<Tensor> ep_routes_cuda(const Tensor& c_all_in, const Tensor& e_sorted, int64_t rank, int64_t cap,
+                                   const std::optional<Tensor>& ret_bases, const std::optional<Tensor>& gret_bases,
+                                   int64_t row_bytes) {
+  TORCH_CHECK(c_all_in.is_cuda() && c_all_in.dim() == 2, "ep_routes: c_all must be a [world, E] CUDA tensor");
+  const c10::cuda::CUDAGuard guard(c_all_in.device());
+  Tensor c_all = c_all_in.to(at::kLong).contiguous();
+  const int64_t world = c_all.size(0), E = c_all.size(1), n = e_sorted.numel();
+  TORCH_CHECK(e_sorted.scalar_type() == at::kLong && e_sorted.is_contiguous(), "ep_routes: e_sorted must be int64");
+  auto opt = c_all.options();
+  Tensor ws = at::empty({mgf_ep_routes_workspace_words(static_cast<int32_t>(world), static_cast<int32_t>(E))},
+                        opt.dtype(at::kInt));
+  Tensor dst_rank = at::empty({n}, opt), dst_row = at::empty({n}, opt);
+  Tensor src_rank = at::empty({cap}, opt), src_pos = at::empty({cap}, opt);
+  Tensor ptr_ret, ptr_gret;
+  const unsigned long long* rb = nullptr;
+  const unsigned long long* gb = nullptr;
+  if (ret_bases.has_value()) {
+    TORCH_CHECK(ret_bases->scalar_type() == at::kLong && ret_bases->numel() == world, "ep_routes: ret_bases [world]");
+    ptr_ret = at::empty({cap}, opt);
+    rb = reinterpret_cast<const unsigned long long*>(ret_bases->data_ptr<int64_t>());
+  }
+  if (gret_bases.has_value()) {
+    TORCH_CHECK(gret_bases->scalar_type() == at::kLong && gret_bases->numel() == world,
+                "ep_routes: gret_bases [world]");
+    ptr_gret = at::empty({cap}, opt);
+    gb = reinterpret_cast<const unsigned long long*>(gret_bases->data_ptr<int64_t>());
+  }
+  Tensor offs = at::empty({E / world}, opt.dtype(at::kInt)), n_recv = at::empty({1}, opt.dtype(at::kInt));
+  check_launch(mgf_ep_routes(c_all.data_ptr<int64_t>(), static_cast<int32_t>(world), static_cast<int32_t>(E),
+                             e_sorted.data_ptr<int64_t>(), n, static_cast<int32_t>(rank), cap, rb, gb, row_bytes,
+                             ws.data_ptr<int32_t>(), dst_rank.data_ptr<int64_t>(), dst_row.data_ptr<int64_t>(),
+                             src_rank.data_ptr<int64_t>(), src_pos.data_ptr<int64_t>(),
+                             ptr_ret.defined() ? ptr_ret.data_ptr<int64_t>() : nullptr,
+                             ptr_gret.defined() ? ptr_gret.data_ptr<int64_t>() : nullptr, offs.data_ptr<int32_t>(),
+                             n_recv.data_ptr<int32_t>(), at::cuda::getCurrentCUDAStream().stream()),
+               "ep_routes");
+  return {dst_rank, dst_row, src_rank, src_pos, offs, n_recv,
+          ptr_ret.defined() ? ptr_ret : at::empty({0}, opt), ptr_gret.defined() ? ptr_gret : at::empty({0}, opt)};
+}
+
 // Wait on the current stream until every slot of this rank's flag array reaches seq (see mgf_wait_flags).
 void wait_flags_cuda(const Tensor& flags, int64_t seq, int64_t timeout_ns) {
   TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kLong && flags.is_contiguous(),
@@ -665,6 +769,12 @@ TORCH_LIBRARY(grouped_mm, m) {
       " Tensor peer_bases, int dst_rows, int ld_dst, int n_max, Tensor? flag_bases=None, Tensor? counter=None,"
       " int seq=0, int rank=0) -> ()");
   m.def("wait_flags(Tensor flags, int seq, int timeout_ns) -> ()");
+  m.def("signal_flags(Tensor flag_bases, int rank, int seq) -> ()");
+  m.def("mm_scatter(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor row_ptrs) -> ()");
+  m.def("ep_sort(Tensor expert_ids, int num_experts, int topk) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  m.def(
+      "ep_routes(Tensor c_all, Tensor e_sorted, int rank, int cap, Tensor? ret_bases, Tensor? gret_bases,"
+      " int row_bytes) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
@@ -681,6 +791,10 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("combine_rows", &combine_rows_cuda);
   m.impl("push_rows", &push_rows_cuda);
   m.impl("wait_flags", &wait_flags_cuda);
+  m.impl("signal_flags", &signal_flags_cuda);
+  m.impl("mm_scatter", &mm_scatter_cuda);
+  m.impl("ep_sort", &ep_sort_cuda);
+  m.impl("ep_routes", &ep_routes_cuda);
   m.impl("mm_downproj",
          [](const Tensor& a, const Tensor& b, const Tensor& offs, const std::optional<Tensor>& bias,
             const Tensor& aux, double alpha, double limit) {

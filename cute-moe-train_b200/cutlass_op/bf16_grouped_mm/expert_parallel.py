@@ -346,8 +346,18 @@ class PeerBuffers:
         torch.ops.grouped_mm.push_rows(src, src_idx, scale, n_dev, dst_rank, dst_row, self.bases[target], dst_rows,
                                        src.shape[1], n_max, self.bases["flags"], self.counters[kind:kind + 1],
                                        self.seq, self.rank)
+        self.wait(self.seq)
+
+    def signal(self) -> int:
+        """Signal, after the stream's earlier work (a scatter-epilogue GEMM that wrote rows into the
+        ranks' buffers), the next sequence number to every rank; returns it for wait()."""
+        self.seq += 1
+        torch.ops.grouped_mm.signal_flags(self.bases["flags"], self.rank, self.seq)
+        return self.seq
+
+    def wait(self, seq: int) -> None:
         with timed("ep_peer_wait"):
-            torch.ops.grouped_mm.wait_flags(self.flags, self.seq, self.WAIT_TIMEOUT_NS)
+            torch.ops.grouped_mm.wait_flags(self.flags, seq, self.WAIT_TIMEOUT_NS)
 
 
 class _PeerState:
@@ -465,9 +475,74 @@ class _PeerCombine(torch.autograd.Function):
         return st.bufs.local["grows"].view(st.cap, g.shape[1]), grad_w, None
 
 
+class _PeerMoE(torch.autograd.Function):
+    """The expert-parallel MoE FFN of the peer transport in one autograd function, with the combine
+    and the dispatch gradient fused into GEMM epilogues.
+
+    forward:  push x's routed copies into the owners' `rows` (+ completion flags) -> up-proj + bias +
+              SwiGLU -> down-proj + bias whose epilogue stores every output row straight into its
+              source rank's `ret` buffer (mgf_gemm_desc.d_row_ptrs, NVLink peer stores) -> signal ->
+              wait -> per-token weighted sum of the k returned rows.
+    backward: push the output gradient (scaled by the router weights) into the owners' `grows` ->
+              down-proj weight + bias gradient -> down-proj dgrad + SwiGLU backward -> up-proj dgrad
+              whose epilogue stores each row's gradient into its source's `gret` -> signal -> up-proj
+              weight + bias gradient (the transfer lands meanwhile) -> wait -> per-token sum of the k
+              gradient rows.
+    Two of the four row transfers per step thus ride inside GEMMs instead of separate pushes."""
+
+    @staticmethod
+    def forward(ctx, x, w_up, b_up, w_down, b_down, w_flat, st):
+        bufs, plan = st.bufs, st.plan
+        offs = plan["offs"]
+        with timed("ep_peer_dispatch"):
+            bufs.push(0, x.contiguous(), st.copy_token, None, None, plan["dst_rank"], plan["dst_row"], "rows",
+                      st.cap, st.n)
+        rows = bufs.local["rows"]
+        with timed("up_swiglu_fwd"):
+            s, aux = torch.ops.grouped_mm.mm_swiglu(rows, w_up, offs, b_up, st.alpha, st.limit)
+        with timed("down_fwd"):
+            torch.ops.grouped_mm.mm_scatter(s, w_down, offs, b_down, plan["ptr_ret"])
+        bufs.wait(bufs.signal())
+        with timed("ep_combine"):
+            out = torch.ops.grouped_mm.combine_rows(bufs.local["ret"], st.inv_order, w_flat, st.k)
+        ctx.save_for_backward(w_up, w_down, s, aux)
+        ctx.w_flat, ctx.st = w_flat, st
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        w_up, w_down, s, aux = ctx.saved_tensors
+        st, w_flat = ctx.st, ctx.w_flat
+        bufs, plan = st.bufs, st.plan
+        offs = plan["offs"]
+        g = g.contiguous()
+        scale = w_flat[st.order].contiguous() if w_flat is not None else None
+        with timed("ep_peer_combine_bwd"):
+            bufs.push(2, g, st.copy_token, scale, None, plan["dst_rank"], plan["dst_row"], "grows", st.cap, st.n)
+        grows = bufs.local["grows"]
+        with timed("down_wgrad_bias"):
+            g_wd, g_bd = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), grows, offs)
+        with timed("down_dgrad_swiglu_bwd"):
+            grad_aux = torch.ops.grouped_mm.mm_swiglu_bwd(grows, w_down.transpose(-2, -1), offs, aux, st.alpha,
+                                                          st.limit)
+        with timed("up_dgrad"):
+            torch.ops.grouped_mm.mm_scatter(grad_aux, w_up.transpose(-2, -1), offs, None, plan["ptr_gret"])
+        seq = bufs.signal()
+        with timed("up_wgrad_bias"):
+            g_wu, g_bu = torch.ops.grouped_mm.mm_wgrad_bias(bufs.local["rows"].transpose(-2, -1), grad_aux, offs)
+        bufs.wait(seq)
+        with timed("ep_combine"):
+            gx = torch.ops.grouped_mm.combine_rows(bufs.local["gret"], st.inv_order, None, st.k)
+        grad_w = None
+        if w_flat is not None and ctx.needs_input_grad[5]:
+            copies = bufs.local["ret"][st.inv_order].float().view(-1, st.k, g.shape[1])
+            grad_w = (copies * g.float().unsqueeze(1)).sum(-1).reshape(-1)
+        return gx, g_wu, g_bu.to(w_up.dtype), g_wd, g_bd.to(w_down.dtype), grad_w, None
+
+
 def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int, expert_fn: Callable,
                     bufs_cache: dict, group=None, router_weights: torch.Tensor | None = None,
-                    overlap: bool = False, capacity_factor: float = 2.0) -> tuple:
+                    overlap: bool = False, capacity_factor: float = 2.0, fused: dict | None = None) -> tuple:
     """Expert-parallel MoE FFN with dispatch/combine as peer-memory pushes (CUDA, world > 1).
 
     Same contract as ep_moe_ffn.  Every rank must pass the same number of tokens.  Each rank can
@@ -475,6 +550,10 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
     that are dropped and MGF_DEV_ROW_OUT_OF_RANGE / MGF_DEV_BAD_OFFS are recorded in the device status
     word, which check_device_status() turns into a RuntimeError.  The receive buffers of one call stay
     live until its backward ran; a second forward before that backward raises.
+
+    fused: {"w_up", "b_up", "w_down", "b_down", "alpha", "limit"} runs the local experts as _PeerMoE
+    (combine and dispatch gradient inside the GEMM epilogues; `expert_fn` and `overlap` unused);
+    None runs `expert_fn` between separate dispatch / combine pushes.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -498,19 +577,27 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
                            "its receive buffers")
     st = _PeerState()
     with timed("ep_plan"):
-        flat = expert_idx.reshape(-1).to(torch.int64)
-        st.order = torch.argsort(flat, stable=True)
-        st.copy_token = torch.div(st.order, k, rounding_mode="floor").contiguous()
-        st.inv_order = _inverse(st.order)
-        counts = torch.bincount(flat, minlength=num_experts)
+        order, inv_order, copy_token, e_sorted, counts = torch.ops.grouped_mm.ep_sort(expert_idx, num_experts, k)
+        st.order, st.inv_order, st.copy_token = order, inv_order, copy_token
         c_all = torch.empty(world, num_experts, dtype=counts.dtype, device=x.device)
         # the count exchange also orders this call after every rank's previous use of the buffers
         dist.all_gather_into_tensor(c_all, counts, group=group)
-        st.plan = push_plan(c_all, flat[st.order], rank, world, e_local, cap)
+        r = torch.ops.grouped_mm.ep_routes(c_all, e_sorted, rank, cap, bufs.bases["ret"], bufs.bases["gret"],
+                                           H * x.element_size())
+        st.plan = {"dst_rank": r[0], "dst_row": r[1], "src_rank": r[2], "src_pos": r[3], "offs": r[4],
+                   "n_recv": r[5], "ptr_ret": r[6], "ptr_gret": r[7]}
     st.bufs, st.k, st.n, st.cap = bufs, k, n, cap
     st.side_stream = bufs.side_stream
     st.dispatch_bwd_done = None
     st.overlap = overlap
+    if fused is not None:
+        st.alpha, st.limit = fused["alpha"], fused["limit"]
+        w_flat = router_weights.reshape(-1).float().contiguous() if router_weights is not None else None
+        out = _PeerMoE.apply(x, fused["w_up"], fused["b_up"], fused["w_down"], fused["b_down"], w_flat, st)
+        bufs.pending_backward = out.requires_grad
+        if out.requires_grad:
+            out.register_hook(lambda g: (setattr(bufs, "pending_backward", False), g)[1])
+        return out, st
     rows = _PeerDispatch.apply(x, st)
     y = expert_fn(rows, st.plan["offs"], st) if getattr(expert_fn, "takes_peer_state", False) else \
         expert_fn(rows, st.plan["offs"])
@@ -527,13 +614,16 @@ class EPMoEFFN(torch.nn.Module):
 
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
                  swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer",
-                 overlap: bool = False, capacity_factor: float = 2.0):
+                 overlap: bool = False, capacity_factor: float = 2.0, fused: bool = True):
         """transport: "peer" (NVLink pushes, CUDA, world > 1) or "nccl" (all-to-all).  overlap (peer
         transport): push the dispatch's gradient on a side stream under the up-projection weight
         gradient instead of after it.  capacity_factor (peer transport): receive buffers hold
         ceil(capacity_factor * tokens * topk) rows per rank (overflow is reported, see
-        ep_moe_ffn_peer)."""
+        ep_moe_ffn_peer).  fused (peer transport): the combine and the dispatch gradient are written by
+        the down-proj forward / up-proj dgrad epilogues straight into the source ranks (_PeerMoE);
+        False: separate push kernels around the FFN (then `overlap` applies)."""
         super().__init__()
+        self.fused = fused
         self.overlap = overlap
         self.capacity_factor = capacity_factor
         if transport not in ("peer", "nccl"):
@@ -572,9 +662,13 @@ class EPMoEFFN(torch.nn.Module):
     def forward(self, x: torch.Tensor, expert_idx: torch.Tensor, router_weights: torch.Tensor | None = None):
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if self.transport == "peer" and world > 1 and x.is_cuda:
+            fused = None
+            if self.fused:
+                fused = {"w_up": self.w_up, "b_up": self.b_up, "w_down": self.w_down, "b_down": self.b_down,
+                         "alpha": self.alpha, "limit": self.limit}
             out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self._peer_expert_fn, self._peer_bufs,
                                       self.group, router_weights, overlap=self.overlap,
-                                      capacity_factor=self.capacity_factor)
+                                      capacity_factor=self.capacity_factor, fused=fused)
             self.last_local_rows = st.plan["n_recv"]  # device tensor; read it outside timed regions
             return out
         out, plan = ep_moe_ffn(x, expert_idx, self.num_experts, self.expert_fn, self.group, router_weights)

@@ -118,6 +118,13 @@ typedef struct mgf_gemm_desc {
   const float* scale_a;  /* E4M3: device fp32 [total_rows] */
   const float* scale_b;  /* E4M3: device fp32 [E, n] */
   int64_t scale_b_stride;
+  const int64_t* d_row_ptrs; /* BIAS (bf16) only, NULL = off.  Scatter mode: output row r is written
+                            at the address d_row_ptrs[r] (device int64 [total_rows]; any address this
+                            device can store to, e.g. a peer GPU's IPC-mapped buffer; 0 = row not
+                            written; 16-byte aligned, 32-byte aligned for whole-sector stores)
+                            instead of d + r * ldd (d and ldd are then unused).  The expert-parallel
+                            combine writes each expert output straight into its source rank's buffer
+                            this way, fusing the transfer into the GEMM epilogue. */
 } mgf_gemm_desc;
 
 enum mgf_ab_type { MGF_AB_BF16 = 0, MGF_AB_E4M3 = 1 };
@@ -178,6 +185,32 @@ int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t*
  * (no counterpart in the reference). */
 int mgf_wait_flags(const unsigned long long* flags, int64_t world, unsigned long long seq, int64_t timeout_ns,
                    void* stream);
+
+/* Signal on `stream`: after every earlier operation of the stream (e.g. a scatter-epilogue GEMM
+ * that stored rows into peers' buffers), write seq into slot `rank` of every rank's flag array
+ * (flag_bases as for mgf_push_rows).  Readers use mgf_wait_flags.  No counterpart in the reference. */
+int mgf_signal_flags(const unsigned long long* flag_bases, int64_t world, int64_t rank, unsigned long long seq,
+                     void* stream);
+
+/* Device-side plan of the expert-parallel peer transport (no counterpart in the reference; no host
+ * synchronisation).  mgf_ep_sort: stable counting sort of n routed copies (expert_ids int64 [n], copy
+ * i = token i / topk) by expert: order[p] (copy at sorted position p), inv_order[copy], copy_token[p],
+ * e_sorted[p], counts[E] (int64).  Out-of-range ids are clamped and set MGF_DEV_ROW_OUT_OF_RANGE.
+ * mgf_ep_routes: from the all-gathered count matrix c_all [world, E] (int64) and this rank's e_sorted:
+ * dst_rank / dst_row [n] (owner rank and row of each sorted copy in the owner's receive buffer: local
+ * expert-major, then source rank, then sorted order), src_rank / src_pos [cap] (source rank and its
+ * sorted position of each receive row; -1 past the received rows), optional ptr_ret / ptr_gret [cap]
+ * (ret_bases[src] + src_pos * row_bytes and the same in gret_bases; 0 past the received rows: the row
+ * addresses of the scatter epilogues), offs [E / world] (int32) and n_recv [1] (int32).  workspace:
+ * int32 [mgf_ep_routes_workspace_words(world, E)] device scratch. */
+int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk, int64_t* order,
+                int64_t* inv_order, int64_t* copy_token, int64_t* e_sorted, int64_t* counts, void* stream);
+int64_t mgf_ep_routes_workspace_words(int32_t world, int32_t num_experts);
+int mgf_ep_routes(const int64_t* c_all, int32_t world, int32_t num_experts, const int64_t* e_sorted, int64_t n,
+                  int32_t rank, int64_t cap, const unsigned long long* ret_bases,
+                  const unsigned long long* gret_bases, int64_t row_bytes, int32_t* workspace, int64_t* dst_rank,
+                  int64_t* dst_row, int64_t* src_rank, int64_t* src_pos, int64_t* ptr_ret, int64_t* ptr_gret,
+                  int32_t* offs, int32_t* n_recv, void* stream);
 
 /* Map a peer process's device allocation (its 64-byte cudaIpcMemHandle_t) into the context of
  * the calling thread's current device, peer access enabled, for mgf_push_rows destinations

@@ -162,9 +162,9 @@ def _transport_worker(rank, world, port, q):
             g0 = torch.randn(T, H, generator=gen).to(torch.bfloat16)
             idx = route_tokens(T, E, K, "zipf", seed=20 + rank)
             res["inputs"] = [x0.float().numpy(), idx.numpy(), w0.numpy(), g0.float().numpy()]
-            for transport in ("nccl", "peer", "peer_overlap"):
+            for transport in ("nccl", "peer", "peer_unfused", "peer_overlap"):
                 ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport.split("_")[0],
-                               overlap=transport.endswith("overlap"))
+                               overlap=transport.endswith("overlap"), fused=transport == "peer")
                 x = x0.to(dev).requires_grad_(True)
                 w = w0.to(dev).requires_grad_(True)
                 for step in range(2):  # the second step reuses the peer buffers
@@ -196,9 +196,11 @@ def _transport_worker(rank, world, port, q):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_world2_every_transport_matches_oracle():
     """Two ranks, Zipf routing, router weights, a random output gradient, two steps: for the NCCL
-    all-to-all, the peer pushes and the peer pushes with the overlapped dispatch gradient, each
-    rank's output, token gradient, router-weight gradient and its experts' weight and bias gradients
-    match the single-process oracle over both ranks' tokens; the overlap changes no bit."""
+    all-to-all, the peer transport with the combine / dispatch gradient fused into the GEMM epilogues
+    (the default), the peer transport with separate pushes, and that with the overlapped dispatch
+    gradient, each rank's output, token gradient, router-weight gradient and its experts' weight and
+    bias gradients match the single-process oracle over both ranks' tokens; the overlap changes no
+    bit, and the fused epilogues give the separate pushes' results bit for bit."""
     import torch.multiprocessing as mp
 
     from oracle.ep_ffn import ep_reference
@@ -228,10 +230,12 @@ def test_ep_world2_every_transport_matches_oracle():
     want = ep_reference([torch.from_numpy(i[0]).to(bf) for i in ins], [torch.from_numpy(i[1]) for i in ins],
                         [torch.from_numpy(i[2]) for i in ins], [torch.from_numpy(i[3]).to(bf) for i in ins], *wts)
     for rank in range(2):
-        for transport in ("nccl", "peer", "peer_overlap"):
+        for transport in ("nccl", "peer", "peer_unfused", "peer_overlap"):
             _check_ep(transport, [torch.from_numpy(a) for a in res[rank][transport]], want, rank, E // 2)
-        for a, b in zip(res[rank]["peer_overlap"], res[rank]["peer"]):
+        for a, b in zip(res[rank]["peer_overlap"], res[rank]["peer_unfused"]):
             assert (a == b).all(), f"rank{rank}: overlap changed the result"
+        for a, b in zip(res[rank]["peer"], res[rank]["peer_unfused"]):
+            assert (a == b).all(), f"rank{rank}: the fused epilogues changed the result"
 
 
 def _overflow_worker(rank, world, port, q):
@@ -298,3 +302,66 @@ def test_ep_world2_capacity_overflow_is_reported():
     for rank in range(2):
         assert res[rank]["status"] & 0x4, res[rank]        # MGF_DEV_ROW_OUT_OF_RANGE
         assert res[rank]["raised"] and res[rank]["after"] == 0, res[rank]
+
+
+@pytest.mark.parametrize("world,E,T,K", [(1, 8, 300, 4), (2, 16, 517, 4), (4, 128, 1000, 4), (8, 256, 333, 8)])
+def test_device_plan_matches_torch_plan(world, E, T, K):
+    """ep_sort is torch's stable argsort by expert; ep_routes gives push_plan's destinations,
+    sources, offs and row count, and the scatter addresses base[src] + src_pos * row_bytes, for every
+    rank of a simulated group (one GPU: no peer memory is touched)."""
+    from cutlass_op.bf16_grouped_mm.expert_parallel import push_plan, route_tokens
+
+    dev = torch.device("cuda", 0)
+    el = E // world
+    idxs = [route_tokens(T, E, K, "zipf", seed=70 + r, device=dev) for r in range(world)]
+    sorts = [torch.ops.grouped_mm.ep_sort(i, E, K) for i in idxs]
+    for i, (order, inv, tok, es, counts) in zip(idxs, sorts):
+        flat = i.reshape(-1)
+        ref = torch.argsort(flat, stable=True)
+        assert torch.equal(order, ref) and torch.equal(tok, ref // K) and torch.equal(es, flat[ref])
+        assert torch.equal(inv[order], torch.arange(flat.numel(), device=dev))
+        assert torch.equal(counts, torch.bincount(flat, minlength=E))
+    c_all = torch.stack([s_[4] for s_ in sorts])
+    cap = T * K * world
+    bases = torch.tensor([(1 << 40) + (r << 32) for r in range(world)], dtype=torch.int64, device=dev)
+    gbases = bases + (1 << 36)
+    for r in range(world):
+        es = sorts[r][3]
+        ref = push_plan(c_all, es, r, world, el, cap)
+        got = torch.ops.grouped_mm.ep_routes(c_all, es, r, cap, bases, gbases, 5760)
+        n_recv = int(ref["n_recv"])
+        assert torch.equal(got[0], ref["dst_rank"]) and torch.equal(got[1], ref["dst_row"])
+        assert torch.equal(got[4], ref["offs"]) and int(got[5]) == n_recv
+        assert torch.equal(got[2][:n_recv], ref["src_rank"][:n_recv])
+        assert torch.equal(got[3][:n_recv], ref["src_pos"][:n_recv])
+        assert (got[2][n_recv:] == -1).all() and (got[6][n_recv:] == 0).all() and (got[7][n_recv:] == 0).all()
+        want = bases[ref["src_rank"][:n_recv]] + ref["src_pos"][:n_recv] * 5760
+        assert torch.equal(got[6][:n_recv], want) and torch.equal(got[7][:n_recv], want + (1 << 36))
+
+
+def test_scatter_epilogue_writes_rows_to_their_addresses():
+    """mm_scatter (BIAS epilogue with per-row destination addresses) stores exactly what the plain
+    operator computes, row by row at the given addresses (a permutation of a local buffer here,
+    32- and 16-byte aligned rows), and leaves rows with address 0 alone."""
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(3, 128, 64, [70, 0, 131], seed=31)
+    s = x[:, :64].contiguous().cuda()
+    wd, bd, offs = w_down.cuda(), b_down.cuda(), offs.cuda()
+    ref = torch.ops.grouped_mm.mm(s, wd, offs, bd, -1)
+    M, H_ = s.shape[0], wd.shape[2]
+    for pitch in (H_, H_ + 8):  # 256-byte rows (32-byte aligned) and 272-byte rows (16-byte aligned)
+        dst = torch.full((M + 5, pitch), float("nan"), dtype=torch.bfloat16, device="cuda")
+        perm = torch.randperm(M + 5, generator=torch.Generator().manual_seed(pitch))[:M].cuda()
+        ptrs = dst.data_ptr() + perm * (pitch * 2)
+        ptrs[7] = 0  # row 7 has no destination
+        torch.ops.grouped_mm.mm_scatter(s, wd, offs, bd, ptrs)
+        torch.cuda.synchronize()
+        got = dst[perm][:, :H_]
+        keep = torch.ones(M, dtype=torch.bool)
+        keep[7] = False
+        assert torch.equal(got[keep.cuda()], ref[keep.cuda()])
+        assert torch.isnan(dst[perm[7]].float()).all()
+    from cutlass_op.bf16_grouped_mm import check_device_status
+
+    check_device_status()
