@@ -338,42 +338,49 @@ extern "C" int mgf_wait_flags(const unsigned long long* flags, int64_t world, un
 namespace mgf {
 namespace {
 
-__global__ void __launch_bounds__(1024) ep_sort_kernel(const int64_t* __restrict__ ids, int64_t n, int E, int k,
-                                                      int64_t* __restrict__ order, int64_t* __restrict__ inv,
-                                                      int64_t* __restrict__ token, int64_t* __restrict__ e_sorted,
-                                                      int64_t* __restrict__ counts, unsigned int* __restrict__ status) {
-  extern __shared__ int sh[];  // hist[32][E], tot[E]
-  int* tot = sh + 32 * E;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t chunk = (n + 31) / 32;
-  const int64_t lo = warp * chunk;
-  const int64_t hi = lo + chunk < n ? lo + chunk : n;
-  int* h = sh + warp * E;
-  for (int e = lane; e < E; e += 32) h[e] = 0;
-  __syncwarp();
-  bool bad = false;
-  for (int64_t i = lo + lane; i < hi; i += 32) {
-    int64_t e = __ldg(ids + i);
-    if (e < 0 || e >= E) {
-      bad = true;
-      e = e < 0 ? 0 : E - 1;
-    }
-    atomicAdd(&h[e], 1);
+// Stable counting sort in three launches.  Copies are cut into blocks of 1024 (32 warps x 32);
+// ep_hist counts each block's copies per expert, ep_scan turns the [block][expert] counts into
+// exclusive starts (expert-major, then block), ep_scatter ranks every copy inside its block (warp
+// by warp, lane by lane: the original order) and writes it to start + rank.
+constexpr int kSortBlock = 1024;
+
+__device__ __forceinline__ int clamp_expert(int64_t r, int E, bool& bad) {
+  if (r < 0 || r >= E) {
+    bad = true;
+    return r < 0 ? 0 : E - 1;
   }
-  if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+  return static_cast<int>(r);
+}
+
+__global__ void __launch_bounds__(kSortBlock) ep_hist_kernel(const int64_t* __restrict__ ids, int64_t n, int E,
+                                                            int* __restrict__ bhist, unsigned int* __restrict__ status) {
+  extern __shared__ int h[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {  // exclusive prefix over warps, per expert
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kSortBlock + threadIdx.x;
+  bool bad = false;
+  if (i < n) atomicAdd(&h[clamp_expert(__ldg(ids + i), E, bad)], 1);
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, MGF_DEV_ROW_OUT_OF_RANGE);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) bhist[static_cast<int64_t>(blockIdx.x) * E + e] = h[e];
+}
+
+__global__ void __launch_bounds__(1024) ep_scan_kernel(int* __restrict__ bhist, int nblocks, int E,
+                                                       int64_t* __restrict__ counts) {
+  extern __shared__ int tot[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {  // exclusive over blocks, per expert
     int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int c = sh[w * E + e];
-      sh[w * E + e] = run;
+    for (int b = 0; b < nblocks; ++b) {
+      const int c = bhist[static_cast<int64_t>(b) * E + e];
+      bhist[static_cast<int64_t>(b) * E + e] = run;
       run += c;
     }
     tot[e] = run;
     counts[e] = run;
   }
   __syncthreads();
-  if (warp == 0) {  // exclusive prefix of the totals over experts (in place)
+  if (threadIdx.x < 32) {  // exclusive prefix of the totals over experts (in place)
+    const int lane = threadIdx.x;
     int carry = 0;
     for (int base = 0; base < E; base += 32) {
       const int e = base + lane;
@@ -389,29 +396,42 @@ __global__ void __launch_bounds__(1024) ep_sort_kernel(const int64_t* __restrict
     }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < 32 * E; idx += blockDim.x) sh[idx] += tot[idx % E];
+  for (int64_t idx = threadIdx.x; idx < static_cast<int64_t>(nblocks) * E; idx += blockDim.x)
+    bhist[idx] += tot[idx % E];
+}
+
+__global__ void __launch_bounds__(kSortBlock) ep_scatter_kernel(const int64_t* __restrict__ ids, int64_t n, int E,
+                                                               int k, const int* __restrict__ bstart,
+                                                               int64_t* __restrict__ order, int64_t* __restrict__ inv,
+                                                               int64_t* __restrict__ token,
+                                                               int64_t* __restrict__ e_sorted) {
+  extern __shared__ int wh[];  // [32 warps][E]: copies of each expert in the block's earlier warps
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int idx = threadIdx.x; idx < 32 * E; idx += blockDim.x) wh[idx] = 0;
   __syncthreads();
-  // in order, 32 copies at a time: rank among the same expert's lanes, then the group's last lane
-  // advances the expert's cursor
-  for (int64_t base = lo; base < hi; base += 32) {
-    const int64_t i = base + lane;
-    const bool v = i < hi;
-    int e = -1;
-    if (v) {
-      const int64_t r = __ldg(ids + i);
-      e = r < 0 ? 0 : (r >= E ? E - 1 : static_cast<int>(r));
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kSortBlock + threadIdx.x;
+  const bool v = i < n;
+  bool bad = false;
+  const int e = v ? clamp_expert(__ldg(ids + i), E, bad) : -1;
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
+  if (v && lane == 31 - __clz(peers)) wh[warp * E + e] = __popc(peers);
+  __syncthreads();
+  for (int c = threadIdx.x; c < E; c += blockDim.x) {  // exclusive over warps, per expert
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int x = wh[w * E + c];
+      wh[w * E + c] = run;
+      run += x;
     }
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    if (v) {
-      const int pos = h[e] + __popc(peers & ((1u << lane) - 1u));
-      order[pos] = i;
-      inv[i] = pos;
-      token[pos] = i / k;
-      e_sorted[pos] = e;
-    }
-    __syncwarp();
-    if (v && lane == 31 - __clz(peers)) h[e] += __popc(peers);
-    __syncwarp();
+  }
+  __syncthreads();
+  if (v) {
+    const int64_t pos = bstart[static_cast<int64_t>(blockIdx.x) * E + e] + wh[warp * E + e] + rank_in_warp;
+    order[pos] = i;
+    inv[i] = pos;
+    token[pos] = i / k;
+    e_sorted[pos] = e;
   }
 }
 
@@ -512,21 +532,33 @@ __global__ void signal_flags_kernel(const unsigned long long* __restrict__ flag_
 }  // namespace
 }  // namespace mgf
 
-extern "C" int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk, int64_t* order,
-                           int64_t* inv_order, int64_t* copy_token, int64_t* e_sorted, int64_t* counts, void* stream) {
+extern "C" int64_t mgf_ep_sort_workspace_words(int64_t n, int32_t num_experts) {
+  const int64_t nb = (n + mgf::kSortBlock - 1) / mgf::kSortBlock;
+  return (nb > 0 ? nb : 1) * num_experts;
+}
+
+extern "C" int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk,
+                           int32_t* workspace, int64_t* order, int64_t* inv_order, int64_t* copy_token,
+                           int64_t* e_sorted, int64_t* counts, void* stream) {
   using namespace mgf;
   if (n < 0 || n > INT32_MAX || num_experts < 1 || num_experts > 1024 || topk < 1) return MGF_ERR_INVALID_ARGUMENT;
-  if (counts == nullptr || (n > 0 && (expert_ids == nullptr || order == nullptr || inv_order == nullptr ||
-                                      copy_token == nullptr || e_sorted == nullptr)))
+  if (counts == nullptr || workspace == nullptr ||
+      (n > 0 && (expert_ids == nullptr || order == nullptr || inv_order == nullptr || copy_token == nullptr ||
+                 e_sorted == nullptr)))
     return MGF_ERR_INVALID_ARGUMENT;
   unsigned int* status = status_word_address();
   if (status == nullptr) return MGF_ERR_CUDA;
-  const int smem = (32 + 1) * num_experts * static_cast<int>(sizeof(int));
-  if (cudaFuncSetAttribute(ep_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nb = static_cast<int>((n + kSortBlock - 1) / kSortBlock);
+  const int smem_h = num_experts * static_cast<int>(sizeof(int));
+  const int smem_w = 32 * num_experts * static_cast<int>(sizeof(int));
+  if (cudaFuncSetAttribute(ep_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_w) != cudaSuccess)
     return MGF_ERR_CUDA;
-  ep_sort_kernel<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(expert_ids, n, num_experts, topk, order,
-                                                                      inv_order, copy_token, e_sorted, counts,
-                                                                      status);
+  if (nb > 0) ep_hist_kernel<<<nb, kSortBlock, smem_h, st>>>(expert_ids, n, num_experts, workspace, status);
+  ep_scan_kernel<<<1, 1024, smem_h, st>>>(workspace, nb, num_experts, counts);
+  if (nb > 0)
+    ep_scatter_kernel<<<nb, kSortBlock, smem_w, st>>>(expert_ids, n, num_experts, topk, workspace, order,
+                                                      inv_order, copy_token, e_sorted);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 

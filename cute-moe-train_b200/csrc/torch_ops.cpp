@@ -676,8 +676,10 @@ std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> ep_sort_cuda(const Tensor& id
   auto opt = ids.options();
   Tensor order = at::empty({n}, opt), inv = at::empty({n}, opt), tok = at::empty({n}, opt),
          es = at::empty({n}, opt), counts = at::empty({num_experts}, opt);
+  Tensor ws = at::empty({mgf_ep_sort_workspace_words(n, static_cast<int32_t>(num_experts))}, opt.dtype(at::kInt));
   check_launch(mgf_ep_sort(ids.data_ptr<int64_t>(), n, static_cast<int32_t>(num_experts),
-                           static_cast<int32_t>(topk), order.data_ptr<int64_t>(), inv.data_ptr<int64_t>(),
+                           static_cast<int32_t>(topk), ws.data_ptr<int32_t>(), order.data_ptr<int64_t>(),
+                           inv.data_ptr<int64_t>(),
                            tok.data_ptr<int64_t>(), es.data_ptr<int64_t>(), counts.data_ptr<int64_t>(),
                            at::cuda::getCurrentCUDAStream().stream()),
                "ep_sort");

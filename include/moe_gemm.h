@@ -195,7 +195,8 @@ int mgf_signal_flags(const unsigned long long* flag_bases, int64_t world, int64_
 /* Device-side plan of the expert-parallel peer transport (no counterpart in the reference; no host
  * synchronisation).  mgf_ep_sort: stable counting sort of n routed copies (expert_ids int64 [n], copy
  * i = token i / topk) by expert: order[p] (copy at sorted position p), inv_order[copy], copy_token[p],
- * e_sorted[p], counts[E] (int64).  Out-of-range ids are clamped and set MGF_DEV_ROW_OUT_OF_RANGE.
+ * e_sorted[p], counts[E] (int64); workspace: int32 [mgf_ep_sort_workspace_words(n, E)] device scratch.
+ * Out-of-range ids are clamped and set MGF_DEV_ROW_OUT_OF_RANGE.
  * mgf_ep_routes: from the all-gathered count matrix c_all [world, E] (int64) and this rank's e_sorted:
  * dst_rank / dst_row [n] (owner rank and row of each sorted copy in the owner's receive buffer: local
  * expert-major, then source rank, then sorted order), src_rank / src_pos [cap] (source rank and its
@@ -203,8 +204,10 @@ int mgf_signal_flags(const unsigned long long* flag_bases, int64_t world, int64_
  * (ret_bases[src] + src_pos * row_bytes and the same in gret_bases; 0 past the received rows: the row
  * addresses of the scatter epilogues), offs [E / world] (int32) and n_recv [1] (int32).  workspace:
  * int32 [mgf_ep_routes_workspace_words(world, E)] device scratch. */
-int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk, int64_t* order,
-                int64_t* inv_order, int64_t* copy_token, int64_t* e_sorted, int64_t* counts, void* stream);
+int64_t mgf_ep_sort_workspace_words(int64_t n, int32_t num_experts);
+int mgf_ep_sort(const int64_t* expert_ids, int64_t n, int32_t num_experts, int32_t topk, int32_t* workspace,
+                int64_t* order, int64_t* inv_order, int64_t* copy_token, int64_t* e_sorted, int64_t* counts,
+                void* stream);
 int64_t mgf_ep_routes_workspace_words(int32_t world, int32_t num_experts);
 int mgf_ep_routes(const int64_t* c_all, int32_t world, int32_t num_experts, const int64_t* e_sorted, int64_t n,
                   int32_t rank, int64_t cap, const unsigned long long* ret_bases,
