@@ -221,7 +221,7 @@ __device__ __forceinline__ void decode_tile(int t, const Params& p, const SchedS
     ti.row_end = 0;
     ti.k_start = s.seg_start[lo];
     ti.k_end = s.seg_end[lo];
-    ti.nk = (ti.k_end - ti.k_start + BK - 1) / BK;
+    ti.nk = (ti.k_end - ti.k_start + p.bke - 1) / p.bke;  // K rows per stage: 64 (bf16) or 128 (e4m3)
   }
 }
 
@@ -324,6 +324,23 @@ __device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, i
   }
 }
 
+// e4m3 variant: every operand chunk of a stage is 128 elements (128 bytes) wide and 128 K rows
+// deep (16 KB); clear the K rows past the group end and put e4m3 1.0 (0x38) into the ones row.
+template <int CHUNKS>
+__device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k, int ones_local, int lane) {
+  for (int u = valid_k * 8 + lane; u < 128 * 8; u += 32) {
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) *reinterpret_cast<uint4*>(sA + c * 16384 + u * 16) = make_uint4(0, 0, 0, 0);
+  }
+  if (ones_local >= 0) {  // A holds 128 features: one chunk; 128-byte swizzle: 16-byte unit ^= row % 8
+    const int mm = ones_local & 127;
+    for (int kr = lane; kr < valid_k; kr += 32) {
+      const int off = kr * 128 + ((((mm >> 4) ^ (kr & 7))) << 4) + (mm & 15);
+      sA[off] = 0x38u;
+    }
+  }
+}
+
 // CG = 1: one CTA per 128 x BN tile.  CG = 2: a cluster of two CTAs per 256 x BN tile; the even
 // CTA issues tcgen05.mma.cta_group::2 over both CTAs' shared memory (each CTA holds 128 rows of A
 // and BN/2 columns of B) and both CTAs' TMEM (each holds its 128 rows of the accumulator).
@@ -336,6 +353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmD, const Params p) {
   using Cfg = TileCfg<BN, CG, B_MN>;
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
+  constexpr int KR = (RAGGED_K && F8) ? 128 : BK;  // ragged-K: token rows per stage
+  static_assert(!(RAGGED_K && F8) || (CG == 1 && (BN == 128 || BN == 256)), "e4m3 weight gradient: single CTA");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int TM = BM * CG;   // rows of a tile
   constexpr int BNC = BN / CG;  // B columns held by one CTA
@@ -425,8 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Stages relayed through the odd CTA (CG = 2, ragged-K): those it must patch before the MMA.
   auto relayed = [&](const TileInfo& ti, int kb, bool odd_ones) -> bool {
     if constexpr (CG == 2 && RAGGED_K) {
-      const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
-      return valid_k < BK || odd_ones;
+      const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
+      return valid_k < KR || odd_ones;
     }
     return false;
   };
@@ -508,6 +527,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               load3(sB, &tmB, kb * BKE, nb0, ti.e);
             }
+          } else if constexpr (F8) {
+            // e4m3 token rows: one {128 features, 128 rows} box per 128 columns of A and of B
+            const int kr = ti.k_start + kb * KR;
+            const int m0 = ti.m_blk * TM;
+            load2(sA, &tmA, m0, kr);
+#pragma unroll
+            for (int c = 0; c < BNC / 128; ++c) load2(sB + c * 16384, &tmB, nb0 + 128 * c, kr);
           } else {
             const int kr = ti.k_start + kb * BK;
             const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
@@ -543,10 +569,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     //                                                              ragged-K stage patcher (odd CTA)
     constexpr uint32_t idesc =
         F8 ? ptx::make_idesc_e4m3(TM, BN, A_MN, B_MN) : ptx::make_idesc_bf16(TM, BN, A_MN, B_MN);
-    constexpr uint32_t a_lbo = A_MN ? 8192u : 16u;
-    constexpr uint32_t b_lbo = B_MN ? 8192u : 16u;
-    constexpr uint32_t a_kstep = A_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
-    constexpr uint32_t b_kstep = B_MN ? (16u * 128u) >> 4 : (16u * 2u) >> 4;
+    // MN-major operands: chunks of 128 bytes along M / N are 8 KB apart (bf16: 64 K rows per chunk)
+    // or 16 KB apart (e4m3 weight gradient: 128 K rows); one instruction advances 16 (bf16) or 32
+    // (e4m3) K rows of 128 bytes.  K-major: 16-byte units, 32 bytes of K per instruction.
+    constexpr uint32_t mn_lbo = (RAGGED_K && F8) ? 16384u : 8192u;
+    constexpr uint32_t mn_kstep = ((F8 ? 32u : 16u) * 128u) >> 4;
+    constexpr uint32_t a_lbo = A_MN ? mn_lbo : 16u;
+    constexpr uint32_t b_lbo = B_MN ? mn_lbo : 16u;
+    constexpr uint32_t a_kstep = A_MN ? mn_kstep : (16u * 2u) >> 4;
+    constexpr uint32_t b_kstep = B_MN ? mn_kstep : (16u * 2u) >> 4;
     const bool issuer = (CG == 1) || leader;
     uint32_t stage = 0, phase = 0;
     uint32_t relay_bits = 0;  // per-stage phase of patch_done (even CTA) / own full (odd CTA) on relayed stages
@@ -611,9 +642,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         if constexpr (RAGGED_K) {
-          const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
-          if (valid_k < BK || ones_local >= 0) {
-            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
+          const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
+          if (valid_k < KR || ones_local >= 0) {
+            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, ones_local, lane);
+            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -778,6 +810,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_units<2>(p.d2 + (int64_t)grow * p.ldd2 + (col0 >> 1), u, (p.n - col0) >> 4, p.d2_v8);
               }
             } else if constexpr (EPI == MGF_EPI_SWIGLU_BWD) {
+              if constexpr (F8) {
+                // dequantise the accumulator (grad_s) before the SwiGLU backward: scale_a of the row
+                // times the group's column scales of B
+                const float sa = __ldg(p.scale_a + grow);
+                const float4* sp = reinterpret_cast<const float4*>(p.scale_b + (int64_t)ti.e * p.scale_b_stride + col0);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  if (col0 + 4 * g < p.n) {
+                    const float4 sb = __ldg(sp + g);
+                    v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) * (sa * sb.x));
+                    v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) * (sa * sb.y));
+                    v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) * (sa * sb.z));
+                    v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) * (sa * sb.w));
+                  }
+                }
+              }
               uint4 cur[8];
 #pragma unroll
               for (int g = 0; g < 8; ++g) cur[g] = aw[g];
@@ -834,6 +882,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t v[32];
               ptx::tmem_ld_32x32b_x32(tbase + c * 32, v);
               ptx::tmem_ld_wait();
+              if constexpr (F8) {
+                // per-feature scales: scale_a of this row's feature (1 for the bias-gradient row),
+                // scale_b of each column
+                const float rs = row_bias ? 1.0f : (m0 + r < p.m ? __ldg(p.scale_a + m0 + r) : 0.0f);
+                const float4* sp = reinterpret_cast<const float4*>(p.scale_b + col0);
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  const float4 sb = (col0 + 4 * g < p.n) ? __ldg(sp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) * (rs * sb.x));
+                  v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) * (rs * sb.y));
+                  v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) * (rs * sb.z));
+                  v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) * (rs * sb.w));
+                }
+              }
 #pragma unroll
               for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(__uint_as_float(v[2 * h]), __uint_as_float(v[2 * h + 1]));
             } else {
@@ -1035,10 +1097,17 @@ static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUten
 template <int BN, int CG>
 static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, const CUtensorMap& tB,
                         const CUtensorMap& tD, const Params& p, int grid, cudaStream_t st) {
-  if (f8) {  // e4m3: ragged-M forward epilogues, both operands K-major
+  if (f8) {  // e4m3: ragged-M epilogues with both operands K-major; the ragged-K weight gradient
+    if (epi == MGF_EPI_WGRAD) {
+      if constexpr (CG == 1 && (BN == 128 || BN == 256))
+        return launch_inst<BN, MGF_EPI_WGRAD, true, true, 1, true>(tA, tB, tD, p, grid, st);
+      return MGF_ERR_INVALID_ARGUMENT;
+    }
     if (b_mn) return MGF_ERR_INVALID_ARGUMENT;
     if (epi == MGF_EPI_BIAS) return launch_inst<BN, MGF_EPI_BIAS, false, false, CG, true>(tA, tB, tD, p, grid, st);
     if (epi == MGF_EPI_SWIGLU) return launch_inst<BN, MGF_EPI_SWIGLU, false, false, CG, true>(tA, tB, tD, p, grid, st);
+    if (epi == MGF_EPI_SWIGLU_BWD)
+      return launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false, CG, true>(tA, tB, tD, p, grid, st);
     return MGF_ERR_INVALID_ARGUMENT;
   }
   switch (epi) {
@@ -1218,10 +1287,10 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   auto ab_stride_ok = [esz](int64_t s) { return s > 0 && (s * esz) % 16 == 0; };
   if (!no_rows && (!ab_stride_ok(g.lda) || !ab_stride_ok(g.ldb))) return MGF_ERR_ALIGNMENT;
   if (f8) {
-    if (ragged_k || g.b_mn_major || (g.epilogue != MGF_EPI_BIAS && g.epilogue != MGF_EPI_SWIGLU) ||
-        g.scale_a == nullptr || g.scale_b == nullptr || g.bias_per_row)
+    if ((!ragged_k && g.b_mn_major) || g.scale_a == nullptr || g.scale_b == nullptr || g.bias_per_row)
       return MGF_ERR_INVALID_ARGUMENT;
-    if (!aligned16(g.scale_b) || (g.scale_b_stride % 4) != 0 || g.scale_b_stride < 0) return MGF_ERR_ALIGNMENT;
+    if (!aligned16(g.scale_b) || (!ragged_k && ((g.scale_b_stride % 4) != 0 || g.scale_b_stride < 0)))
+      return MGF_ERR_ALIGNMENT;
   }
   p.bke = f8 ? 128 : BK;
   p.scale_a = g.scale_a;
@@ -1285,16 +1354,27 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     p.m = static_cast<int>(g.m);
     p.n = static_cast<int>(g.n);
     p.k = 0;
-    bn = pick_bn(g.n);
+    bn = f8 ? (g.n <= 128 ? 128 : 256) : pick_bn(g.n);  // e4m3: whole 128-column chunks of B
     n_tiles = static_cast<int>((g.n + bn - 1) / bn);
     p.n_tiles = n_tiles;
-    cg = pick_cta_group(true, g.total_rows, g.num_groups, g.m);
+    cg = f8 ? 1 : pick_cta_group(true, g.total_rows, g.num_groups, g.m);
     const int tm = BM * cg;
     p.m_tiles_real = static_cast<int>((g.m + tm - 1) / tm);
     p.bias_grad = g.d2 != nullptr ? 1 : 0;
     p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % tm) == 0) ? 1 : 0);
     const uint32_t box[2] = {64, 64};
-    if (!no_rows) {
+    if (!no_rows && f8) {
+      // e4m3 token rows (row pitches in bytes): {128 features, 128 rows} boxes of A and B
+      const uint32_t box8[2] = {128, 128};
+      const uint64_t dA[2] = {static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.total_rows)};
+      const uint64_t sA[1] = {static_cast<uint64_t>(g.lda)};
+      const uint64_t dB[2] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.total_rows)};
+      const uint64_t sB[1] = {static_cast<uint64_t>(g.ldb)};
+      if (!encode_bf16(&tA, g.a, 2, dA, sA, box8, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_DATA_TYPE_UINT8) ||
+          !encode_bf16(&tB, g.b, 2, dB, sB, box8, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_DATA_TYPE_UINT8))
+        return MGF_ERR_CUDA;
+      p.a_chunked = p.b_chunked = 0;
+    } else if (!no_rows) {
       // Where the feature count is a multiple of 64, a stage's 64-column chunks of an operand come
       // in one 3D box: {64 features, 64 rows, chunks}, the chunk dimension 128 bytes apart (TMA
       // clips it at the last chunk, so the m / n tails still read as zeros).  Otherwise one 2D box

@@ -428,7 +428,7 @@ Tensor mm_downproj_cuda(const Tensor& mat_a, const Tensor& mat_b, const std::opt
 // and the epilogue; outputs are bf16 exactly as in mm / mm_swiglu.
 void launch_ragged_m_f8(int epi, const Tensor& a, const Tensor& b, const Tensor& offs, const Tensor& scale_a,
                         const Tensor& scale_b, const Tensor* bias, const Tensor& d, const Tensor* d2, double alpha,
-                        double limit, bool store_aux, const char* what) {
+                        double limit, bool store_aux, const char* what, const Tensor* aux = nullptr) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && scale_a.is_cuda() && scale_b.is_cuda(), what,
               ": inputs must be CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, what,
@@ -476,11 +476,88 @@ void launch_ragged_m_f8(int epi, const Tensor& a, const Tensor& b, const Tensor&
     g.d2 = d2->data_ptr();
     g.ldd2 = d2->stride(0);
   }
+  if (aux != nullptr) {
+    g.aux = aux->data_ptr();
+    g.ld_aux = aux->stride(0);
+  }
   g.swiglu_alpha = static_cast<float>(alpha);
   g.swiglu_limit = static_cast<float>(limit);
   g.store_aux = store_aux ? 1 : 0;
   g.sm_carveout = sm_carveout_for(a);
   check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
+}
+
+// e4m3 down-proj dgrad + SwiGLU backward: grad_aux = SwiGLU_bwd(dequant(grad_output @ down_w_t), aux),
+// grad_output e4m3 [M, H] with row scales, down_w_t e4m3 [E, H, I] with unit stride along H and
+// per-(expert, column) scales; aux and grad_aux bf16 [M, 2I] interleaved (gate, up).
+Tensor mm_swiglu_bwd_fp8_cuda(const Tensor& grad_output, const Tensor& down_w_t, const Tensor& offs, const Tensor& aux,
+                              const Tensor& scale_a, const Tensor& scale_b, double alpha, double limit) {
+  const c10::cuda::CUDAGuard guard(grad_output.device());
+  const int64_t I = down_w_t.size(2);
+  TORCH_CHECK(aux.is_cuda() && aux.dim() == 2 && aux.scalar_type() == at::kBFloat16 && aux.stride(1) == 1 &&
+                  aux.size(0) == grad_output.size(0) && aux.size(1) == 2 * I,
+              "grouped_mm_swiglu_bwd_fp8: aux_biased_acc must be bf16 [M, 2*I] row-major");
+  TORCH_CHECK(I % 8 == 0, "grouped_mm_swiglu_bwd_fp8: I must be a multiple of 8");
+  Tensor grad = at::empty_strided({grad_output.size(0), 2 * I}, {padded(2 * I), 1}, aux.options());
+  launch_ragged_m_f8(MGF_EPI_SWIGLU_BWD, grad_output, down_w_t, offs, scale_a, scale_b, nullptr, grad, nullptr, alpha,
+                     limit, false, "grouped_mm_swiglu_bwd_fp8", &aux);
+  return grad;
+}
+
+// e4m3 ragged-K weight gradient with the fused bias gradient: mat_a e4m3 [m, total] (the transposed
+// view of a row-major [total, m]), mat_b e4m3 [total, n] row-major; per-feature fp32 scales
+// scale_a [m] and scale_b [n]; dW[e] = (mat_a[:, rows(e)] @ mat_b[rows(e)]) * scale_a[:, None] * scale_b
+// and db[e] = column sums of mat_b[rows(e)] * scale_b, both bf16.
+std::tuple<Tensor, Tensor> mm_wgrad_fp8_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
+                                             const Tensor& scale_a, const Tensor& scale_b, bool bias_grad) {
+  const char* what = "grouped_mm_wgrad_fp8";
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  TORCH_CHECK(mat_a.scalar_type() == at::kFloat8_e4m3fn && mat_b.scalar_type() == at::kFloat8_e4m3fn, what,
+              ": mat_a and mat_b must be float8_e4m3fn");
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 2 && mat_a.stride(0) == 1 && mat_b.stride(1) == 1, what,
+              ": mat_a must be the transposed view of a row-major [total, m] and mat_b row-major [total, n]");
+  TORCH_CHECK(mat_a.stride(1) % 16 == 0 && mat_b.stride(0) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(mat_a.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(mat_b.data_ptr()) % 16 == 0,
+              what, ": 16-byte aligned bases and row pitches");
+  TORCH_CHECK(mat_a.size(1) == mat_b.size(0), "contraction dimension of mat_a and mat_b must match");
+  check_offs(offs, mat_b);
+  const int64_t E = offs.size(0), M = mat_a.size(0), N = mat_b.size(1);
+  TORCH_CHECK(N % 8 == 0, what, ": n must be a multiple of 8");
+  TORCH_CHECK(scale_a.is_cuda() && scale_a.scalar_type() == at::kFloat && scale_a.is_contiguous() &&
+                  scale_a.numel() == M && scale_b.is_cuda() && scale_b.scalar_type() == at::kFloat &&
+                  scale_b.is_contiguous() && scale_b.numel() == N,
+              what, ": scale_a [m] and scale_b [n] contiguous float32");
+  auto opts = scale_a.options().dtype(at::kBFloat16);
+  Tensor out = at::empty_strided({E, M, N}, {M * padded(N), padded(N), 1}, opts);
+  Tensor db;
+  mgf_gemm_desc g = base_desc();
+  g.epilogue = MGF_EPI_WGRAD;
+  g.ab_type = MGF_AB_E4M3;
+  g.num_groups = static_cast<int32_t>(E);
+  g.total_rows = mat_a.size(1);
+  g.m = M;
+  g.n = N;
+  g.a = mat_a.data_ptr();
+  g.lda = mat_a.stride(1);
+  g.b = mat_b.data_ptr();
+  g.ldb = mat_b.stride(0);
+  g.offs = offs.data_ptr<int32_t>();
+  g.scale_a = scale_a.data_ptr<float>();
+  g.scale_b = scale_b.data_ptr<float>();
+  g.d = out.data_ptr();
+  g.ldd = out.stride(1);
+  g.ldd_batch = out.stride(0);
+  Tensor workspace = at::zeros({1}, offs.options());
+  g.workspace = workspace.data_ptr<int32_t>();
+  if (bias_grad) {
+    db = at::empty({E, N}, opts);
+    g.d2 = db.data_ptr();
+    g.ldd2 = db.stride(0);
+  }
+  g.sm_carveout = sm_carveout_for(mat_b);
+  check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
+  return {out, db};
 }
 
 Tensor mm_fp8_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& scale_a,
@@ -764,6 +841,12 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def(
       "mm_swiglu_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor bias,"
       " float swiglu_alpha, float swiglu_limit) -> (Tensor, Tensor)");
+  m.def(
+      "mm_swiglu_bwd_fp8(Tensor grad_output, Tensor down_w_t, Tensor offs, Tensor aux_biased_acc, Tensor scale_a,"
+      " Tensor scale_b, float swiglu_alpha, float swiglu_limit) -> Tensor");
+  m.def(
+      "mm_wgrad_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, bool bias_grad)"
+      " -> (Tensor, Tensor)");
   m.def("gather_rows(Tensor src, Tensor idx, Tensor? scale) -> Tensor");
   m.def("combine_rows(Tensor rows, Tensor pos, Tensor? weights, int k) -> Tensor");
   m.def(
@@ -789,6 +872,8 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);
   m.impl("mm_fp8", &mm_fp8_cuda);
   m.impl("mm_swiglu_fp8", &mm_swiglu_fp8_cuda);
+  m.impl("mm_swiglu_bwd_fp8", &mm_swiglu_bwd_fp8_cuda);
+  m.impl("mm_wgrad_fp8", &mm_wgrad_fp8_cuda);
   m.impl("gather_rows", &gather_rows_cuda);
   m.impl("combine_rows", &combine_rows_cuda);
   m.impl("push_rows", &push_rows_cuda);

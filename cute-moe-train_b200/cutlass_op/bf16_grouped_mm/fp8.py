@@ -1,14 +1,24 @@
-"""Forward-only FP8 (e4m3) variants of the ragged-M grouped GEMMs: ``grouped_mm::mm_fp8`` (+ bias) and
-``grouped_mm::mm_swiglu_fp8`` (+ bias + clamped SwiGLU, returning ``(swiglu_out, aux_biased_acc)``).
+"""FP8 (e4m3) variants of all four fused epilogues of the MoE FFN, and the FFN with autograd on them.
 
-The reference lists FP8 on its roadmap (README.md:99-102) without fixing a recipe; this one is
-row-wise scaling: every token row of A has an fp32 scale, every output column of every expert's B has
-one, the tensor cores accumulate e4m3 x e4m3 products in fp32 (``tcgen05.mma kind::f8f6f4``), and the
-epilogue multiplies the accumulator by ``scale_a[row] * scale_b[e, col]`` before the bf16 bias and
-SwiGLU -- the same epilogues, and the same bf16 outputs, as the bf16 operators.
+The reference lists FP8 on its roadmap (README.md:99-102) without fixing a recipe; this one scales
+per row for the ragged-M GEMMs and per feature column for the ragged-K weight gradients:
 
-B is taken as ``[E, K, N]`` with unit stride along K, i.e. the transpose of a contiguous [E, N, K]
-tensor (``quantize_weights`` produces it).  Gradients are not defined for these operators.
+* ``grouped_mm::mm_fp8`` (+ bias) and ``grouped_mm::mm_swiglu_fp8`` (+ bias + clamped SwiGLU):
+  every token row of A has an fp32 scale, every output column of every expert's B has one, the tensor
+  cores accumulate e4m3 x e4m3 products in fp32 (``tcgen05.mma kind::f8f6f4``) and the epilogue
+  multiplies the accumulator by ``scale_a[row] * scale_b[e, col]`` before the bf16 bias and SwiGLU;
+* ``grouped_mm::mm_swiglu_bwd_fp8``: the down-proj dgrad with the same row / column scales, the
+  dequantised accumulator going into the SwiGLU backward against the bf16 aux;
+* ``grouped_mm::mm_wgrad_fp8``: the ragged-K weight gradient (+ bias gradient) over token rows.  The
+  contraction runs over tokens, so a per-token scale cannot be factored out; both operands are scaled
+  per feature column instead (``quantize_cols``: one scale per column over all tokens), and the
+  epilogue multiplies by ``scale_a[i] * scale_b[j]`` (the bias-gradient row by ``scale_b[j]``).
+
+B of the ragged-M operators is ``[E, K, N]`` with unit stride along K, i.e. the transpose of a
+contiguous [E, N, K] tensor (``quantize_weights`` produces it).  ``grouped_mm_ffn_fp8`` chains them
+into the fused MoE FFN with autograd: forward ``x -> mm_swiglu_fp8 -> mm_fp8``, backward
+``mm_wgrad_fp8`` (down), ``mm_swiglu_bwd_fp8``, ``mm_fp8`` (up dgrad), ``mm_wgrad_fp8`` (up); every
+output and gradient is bf16, every GEMM operand is quantised right before its GEMM.
 """
 
 from __future__ import annotations
@@ -27,6 +37,24 @@ def _mm_fp8_fake(mat_a, mat_b, offs, scale_a, scale_b, bias):
     n = mat_b.size(-1)
     return torch.empty_strided((mat_a.size(0), n), (_padded(n, torch.bfloat16), 1), dtype=torch.bfloat16,
                                device=mat_a.device)
+
+
+@torch.library.register_fake("grouped_mm::mm_swiglu_bwd_fp8")
+def _mm_swiglu_bwd_fp8_fake(grad_output, down_w_t, offs, aux_biased_acc, scale_a, scale_b, swiglu_alpha,
+                            swiglu_limit):
+    n = 2 * down_w_t.size(-1)
+    return torch.empty_strided((grad_output.size(0), n), (_padded(n, torch.bfloat16), 1), dtype=torch.bfloat16,
+                               device=grad_output.device)
+
+
+@torch.library.register_fake("grouped_mm::mm_wgrad_fp8")
+def _mm_wgrad_fp8_fake(mat_a, mat_b, offs, scale_a, scale_b, bias_grad):
+    e, m, n = offs.size(0), mat_a.size(0), mat_b.size(1)
+    pn = _padded(n, torch.bfloat16)
+    dw = torch.empty_strided((e, m, n), (m * pn, pn, 1), dtype=torch.bfloat16, device=mat_a.device)
+    db = torch.empty((e, n), dtype=torch.bfloat16, device=mat_a.device) if bias_grad else \
+        torch.empty(0, dtype=torch.bfloat16, device=mat_a.device)
+    return dw, db
 
 
 @torch.library.register_fake("grouped_mm::mm_swiglu_fp8")
@@ -62,6 +90,23 @@ def quantize_weights(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return qt.transpose(1, 2), scale.contiguous()
 
 
+def quantize_cols(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [K] scales): x ~= q * scale[None, :]
+    (one scale per feature column over all rows: the weight-gradient operands)."""
+    amax = x.detach().abs().amax(dim=0).float().clamp_min(1e-12) if x.shape[0] else \
+        torch.ones(x.shape[1], device=x.device)
+    scale = amax / E4M3_MAX
+    k = x.shape[1]
+    kp = (k + 15) // 16 * 16
+    q = torch.empty_strided((x.shape[0], k), (kp, 1), dtype=torch.float8_e4m3fn, device=x.device)
+    q.copy_((x.float() / scale[None, :]).clamp_(-E4M3_MAX, E4M3_MAX))
+    return q, scale.contiguous()
+
+
+def dequantize_cols(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    return q.float() * scale[None, :]
+
+
 def dequantize_rows(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     return q.float() * scale[:, None]
 
@@ -84,3 +129,66 @@ def grouped_mm_swiglu_fp8(mat_a: torch.Tensor, mat_b: torch.Tensor, offs: torch.
     with timed("fp8_up_swiglu_fwd"):
         return torch.ops.grouped_mm.mm_swiglu_fp8(mat_a, mat_b, offs, scale_a, scale_b, bias, swiglu_alpha,
                                                   swiglu_limit)
+
+
+def grouped_mm_swiglu_bwd_fp8(grad_output: torch.Tensor, down_w_t: torch.Tensor, offs: torch.Tensor,
+                              aux_biased_acc: torch.Tensor, scale_a: torch.Tensor, scale_b: torch.Tensor,
+                              swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0) -> torch.Tensor:
+    """e4m3 down-proj dgrad + SwiGLU backward -> grad_aux bf16 [total_M, 2I] (interleaved)."""
+    with timed("fp8_down_dgrad_swiglu_bwd"):
+        return torch.ops.grouped_mm.mm_swiglu_bwd_fp8(grad_output, down_w_t, offs, aux_biased_acc, scale_a, scale_b,
+                                                      swiglu_alpha, swiglu_limit)
+
+
+def grouped_mm_wgrad_fp8(a_cols: torch.Tensor, b_cols: torch.Tensor, offs: torch.Tensor, scale_a: torch.Tensor,
+                         scale_b: torch.Tensor, bias_grad: bool = True) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """e4m3 ragged-K weight gradient: a_cols e4m3 [total, m] and b_cols e4m3 [total, n] (row-major token rows,
+    per-column scales from quantize_cols) -> (dW bf16 [E, m, n], db bf16 [E, n] or None)."""
+    with timed("fp8_wgrad_bias"):
+        dw, db = torch.ops.grouped_mm.mm_wgrad_fp8(a_cols.transpose(0, 1), b_cols, offs, scale_a, scale_b, bias_grad)
+    return dw, (db if bias_grad else None)
+
+
+class _FFNFp8(torch.autograd.Function):
+    """The fused MoE FFN with every GEMM in e4m3 (see the module docstring for the recipe)."""
+
+    @staticmethod
+    def forward(ctx, x, w_up, b_up, w_down, b_down, offs, alpha, limit):
+        qx, sx = quantize_rows(x)
+        qwu, swu = quantize_weights(w_up)
+        s, aux = grouped_mm_swiglu_fp8(qx, qwu, offs, sx, swu, b_up, alpha, limit)
+        qs, ss = quantize_rows(s)
+        qwd, swd = quantize_weights(w_down)
+        out = grouped_mm_fp8(qs, qwd, offs, ss, swd, b_down)
+        ctx.save_for_backward(x, w_up, w_down, s, aux, offs)
+        ctx.alpha, ctx.limit = alpha, limit
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w_up, w_down, s, aux, offs = ctx.saved_tensors
+        g = g.contiguous()
+        # down-proj weight + bias gradients over token rows (per-column scales)
+        qs_c, ss_c = quantize_cols(s)
+        qg_c, sg_c = quantize_cols(g)
+        g_wd, g_bd = grouped_mm_wgrad_fp8(qs_c, qg_c, offs, ss_c, sg_c)
+        # down-proj dgrad + SwiGLU backward (row scales for grad_out, column scales for W_down^T)
+        qg, sg = quantize_rows(g)
+        qwdt, swdt = quantize_weights(w_down.transpose(-2, -1))
+        grad_aux = grouped_mm_swiglu_bwd_fp8(qg, qwdt, offs, aux, sg, swdt, ctx.alpha, ctx.limit)
+        # up-proj dgrad and weight + bias gradients
+        qga, sga = quantize_rows(grad_aux)
+        qwut, swut = quantize_weights(w_up.transpose(-2, -1))
+        g_x = grouped_mm_fp8(qga, qwut, offs, sga, swut, None)
+        qx_c, sx_c = quantize_cols(x)
+        qga_c, sga_c = quantize_cols(grad_aux)
+        g_wu, g_bu = grouped_mm_wgrad_fp8(qx_c, qga_c, offs, sx_c, sga_c)
+        return g_x, g_wu, g_bu, g_wd, g_bd, None, None, None
+
+
+def grouped_mm_ffn_fp8(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, offs: torch.Tensor,
+                       b_up: torch.Tensor, b_down: torch.Tensor, swiglu_alpha: float = 1.702,
+                       swiglu_limit: float = 7.0) -> torch.Tensor:
+    """The MoE FFN (up-proj + bias + clamped SwiGLU, down-proj + bias) with every GEMM of its forward and
+    backward in e4m3; bf16 inputs, parameters, output and gradients."""
+    return _FFNFp8.apply(x, w_up, b_up, w_down, b_down, offs, swiglu_alpha, swiglu_limit)

@@ -111,12 +111,16 @@ typedef struct mgf_gemm_desc {
   int32_t bias_per_row;  /* BIAS, ragged-M only: 0 = bias[e, col] added to every row (the MoE case);
                             1 = bias[e, row - group start] added to every column of a row (the
                             transposed form of the reference's ragged-N bias, csrc/grouped_mm_common.cuh:107-118) */
-  int32_t ab_type;       /* enum mgf_ab_type: element type of A and B.  MGF_AB_E4M3 (8-bit float,
-                            BIAS and SWIGLU only, B with unit stride along k): the accumulator is
-                            scaled by scale_a[row] * scale_b[e * scale_b_stride + col] before the
-                            bias; lda / ldb / ldb_batch then count bytes (multiples of 16). */
-  const float* scale_a;  /* E4M3: device fp32 [total_rows] */
-  const float* scale_b;  /* E4M3: device fp32 [E, n] */
+  int32_t ab_type;       /* enum mgf_ab_type: element type of A and B.  MGF_AB_E4M3 (8-bit float).
+                            Ragged-M (BIAS, SWIGLU, SWIGLU_BWD; B with unit stride along k): the
+                            accumulator is scaled by scale_a[row] * scale_b[e * scale_b_stride + col]
+                            before the bias / SwiGLU / SwiGLU backward.  Ragged-K (WGRAD): A and B are
+                            the same row-major token layouts as for bf16, with per-feature scales:
+                            D[e][i][j] = acc * scale_a[i] * scale_b[j], the bias gradient acc * scale_b[j]
+                            (scale_b_stride unused).  lda / ldb / ldb_batch then count bytes
+                            (multiples of 16). */
+  const float* scale_a;  /* E4M3: device fp32 [total_rows] (ragged-M) or [m] (ragged-K) */
+  const float* scale_b;  /* E4M3: device fp32 [E, n] (ragged-M) or [n] (ragged-K) */
   int64_t scale_b_stride;
   const int64_t* d_row_ptrs; /* BIAS (bf16) only, NULL = off.  Scatter mode: output row r is written
                             at the address d_row_ptrs[r] (device int64 [total_rows]; any address this

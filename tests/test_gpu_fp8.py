@@ -66,3 +66,89 @@ def test_fp8_rejects_bad_layouts():
     offs = torch.tensor([16, 32], dtype=torch.int32, device="cuda")
     with pytest.raises(RuntimeError, match="unit stride along K"):
         fp8.grouped_mm_fp8(qx, qw_mn, offs, torch.ones(32, device="cuda"), torch.ones(2, 32, device="cuda"))
+
+
+@pytest.mark.parametrize("cg", ["1", "2"])
+@pytest.mark.parametrize("E,H,I,counts", [(4, 256, 192, [70, 0, 131, 5]), (2, 2880, 256, [1029, 640])])
+def test_fp8_swiglu_bwd(cg, E, H, I, counts, monkeypatch):
+    """e4m3 down-proj dgrad + SwiGLU backward against the fp32 SwiGLU backward of the dequantised GEMM."""
+    import cutlass_op.bf16_grouped_mm as m
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    monkeypatch.setenv("MGF_CTA_GROUP", cg)
+    g = torch.Generator().manual_seed(E + H)
+    M = sum(counts)
+    gout = torch.randn(M, H, generator=g)
+    w_down = torch.randn(E, I, H, generator=g) / I ** 0.5
+    aux = (torch.randn(M, 2 * I, generator=g) * 3).to(torch.bfloat16)
+    offs = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0).to(torch.int32)
+    qg, sg = fp8.quantize_rows(gout.cuda())
+    qw, sw = fp8.quantize_weights(w_down.cuda().transpose(-2, -1))
+    got = fp8.grouped_mm_swiglu_bwd_fp8(qg, qw, offs.cuda(), aux.cuda(), sg, sw)
+    torch.cuda.synchronize()
+    m.check_device_status()
+    # the kernel feeds the fp32 accumulator (not a bf16-rounded one) into the SwiGLU backward
+    gs32 = torch.zeros(M, I)
+    for e, (s0, s1) in enumerate(O.segments(offs)):
+        gs32[s0:s1] = fp8.dequantize_rows(qg, sg).cpu()[s0:s1] @ fp8.dequantize_weights(qw, sw).cpu()[e]
+    ref = O._bf16(O.swiglu_bwd(gs32, aux.float()))
+    rows = int(offs[-1])
+    _check("swiglu_bwd_fp8", got[:rows], ref[:rows])
+
+
+@pytest.mark.parametrize("m_,n,counts", [
+    (192, 320, [70, 0, 131, 5, 1, 129, 256]),   # ones row inside the last m tile, an n tail
+    (256, 256, [300, 7, 0, 129]),               # m % 128 == 0: the ones row gets its own m tile
+    (2880, 5760, [1029, 0, 640, 1]),            # GPT-OSS widths
+])
+def test_fp8_wgrad_bias(m_, n, counts):
+    """e4m3 ragged-K weight + bias gradient against fp32 on the per-column-dequantised operands;
+    empty groups give exact zeros."""
+    import cutlass_op.bf16_grouped_mm as m
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    g = torch.Generator().manual_seed(m_ + n)
+    M = sum(counts)
+    a = torch.randn(M, m_, generator=g)
+    b = torch.randn(M, n, generator=g) * torch.linspace(0.1, 3.0, n)
+    offs = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0).to(torch.int32)
+    qa, sa = fp8.quantize_cols(a.cuda())
+    qb, sb = fp8.quantize_cols(b.cuda())
+    dw, db = fp8.grouped_mm_wgrad_fp8(qa, qb, offs.cuda(), sa, sb)
+    torch.cuda.synchronize()
+    m.check_device_status()
+    ad, bd = fp8.dequantize_cols(qa, sa).cpu(), fp8.dequantize_cols(qb, sb).cpu()
+    ref_w, ref_b = O.grouped_wgrad(ad, bd, offs)
+    for e, (s0, s1) in enumerate(O.segments(offs)):
+        if s1 == s0:
+            assert torch.count_nonzero(dw[e]) == 0 and torch.count_nonzero(db[e]) == 0
+        else:
+            _check(f"dW[{e}]", dw[e], ref_w[e])
+            _check(f"db[{e}]", db[e], ref_b[e])
+
+
+def test_fp8_ffn_tracks_the_bf16_oracle():
+    """grouped_mm_ffn_fp8 (every forward and backward GEMM in e4m3) against the bf16 oracle chain:
+    e4m3 keeps ~3 significant bits less than bf16, so the tolerance here is max|err|/max|ref| <= 0.1
+    and float64 cosine >= 0.995 on the output and all five gradients."""
+    import cutlass_op.bf16_grouped_mm as m
+    from cutlass_op.bf16_grouped_mm import fp8
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(4, 256, 128, [96, 0, 131, 29], seed=12)
+    leaves = [t.cuda().clone().requires_grad_(True) for t in (x, w_up, b_up, w_down, b_down)]
+    out = fp8.grouped_mm_ffn_fp8(leaves[0], leaves[1], leaves[3], offs.cuda(), leaves[2], leaves[4])
+    out.backward(gout.cuda())
+    torch.cuda.synchronize()
+    m.check_device_status()
+    ref = O.kernel_chain(x, w_up, b_up, w_down, b_down, offs, gout)
+    got = dict(zip(["out", "dx", "dw_up", "db_up", "dw_down", "db_down"], [out.detach()] + [t.grad for t in leaves]))
+    rows = int(offs[-1])
+    for k, v in got.items():
+        a, b = v.float().cpu(), ref[k]
+        if k in ("out", "dx"):
+            a, b = a[:rows], b[:rows]
+        r = O.check(k, a, b, rel_tol=0.1, cos_tol=0.995)
+        assert r["ok"], r
+    for k in ("dw_up", "db_up", "dw_down", "db_down"):
+        assert torch.count_nonzero(got[k][1]) == 0
