@@ -736,6 +736,17 @@ def main():
     }
     if ep_parity is not None:
         line["ep_parity"] = ep_parity
+    if world > 1 and ops:
+        # step time split by kind, rank 0's view: grouped GEMMs vs expert-parallel plan / row movement /
+        # waits; the GEMM time scaled to the max SM clock separates clock from communication effects
+        gemm = sum(v["total_ms"] for k, v in ops.items() if k in OP_FLOP_UNITS) / args.steps
+        comm = sum(v["total_ms"] for k, v in ops.items() if k.startswith("ep_")) / args.steps
+        mhz = (clocks or {}).get("sm_mhz")
+        line["ep_breakdown"] = {
+            "gemm_ms_per_step": gemm, "ep_ms_per_step": comm, "other_ms_per_step": ms - gemm - comm,
+            "sm_mhz_median": mhz,
+            "gemm_ms_at_max_clock": gemm * mhz / 1965.0 if mhz else None,
+            "ep_ops_ms": {k: round(v["avg_ms"], 4) for k, v in ops.items() if k.startswith("ep_")}}
 
     # torch._grouped_mm + eager bias/SwiGLU on the same inputs (single GPU only)
     if world == 1 and not args.no_compare and not args.fp8:

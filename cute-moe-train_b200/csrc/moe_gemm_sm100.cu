@@ -301,15 +301,17 @@ __device__ __forceinline__ uint32_t swiglu_bwd_word(float gs, uint32_t aux_word,
   return pack_bf16x2(d_gate, d_up);
 }
 
-// Zero the K rows past the group end in this CTA's A and B chunks of one stage (each K row is one
-// 128-byte line of a 64-column chunk, whatever the swizzle) and set the bias-gradient "ones" row of
-// A for the valid K rows.  Run by one warp; the caller fences the writes to the async proxy.
+// Zero the K rows valid_k..end_k-1 (past the group end, up to the last row the MMAs read) in this
+// CTA's A and B chunks of one stage (each K row is one 128-byte line of a 64-column chunk, whatever
+// the swizzle) and set the bias-gradient "ones" row of A for the valid K rows.  Run by one warp; the
+// caller fences the writes to the async proxy.
 template <int A_CHUNKS, int B_CHUNKS>
-__device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, int ones_local, int lane) {
+__device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, int end_k, int ones_local,
+                                                     int lane) {
   constexpr int kChunks = A_CHUNKS + B_CHUNKS;
-  // 16-byte unit u of a chunk is K row u / 8 (8 units per 128-byte row): clear units 8*valid_k..511
-  // of every chunk, the same unit of all chunks per iteration (the chunks are 8 KB apart).
-  for (int u = valid_k * 8 + lane; u < BK * 8; u += 32) {
+  // 16-byte unit u of a chunk is K row u / 8 (8 units per 128-byte row): clear units
+  // 8*valid_k..8*end_k-1 of every chunk, the same unit of all chunks per iteration (8 KB apart).
+  for (int u = valid_k * 8 + lane; u < end_k * 8; u += 32) {
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) *reinterpret_cast<uint4*>(sA + c * 8192 + u * 16) = make_uint4(0, 0, 0, 0);
   }
@@ -327,8 +329,9 @@ __device__ __forceinline__ void patch_ragged_k_stage(uint8_t* sA, int valid_k, i
 // e4m3 variant: every operand chunk of a stage is 128 elements (128 bytes) wide and 128 K rows
 // deep (16 KB); clear the K rows past the group end and put e4m3 1.0 (0x38) into the ones row.
 template <int CHUNKS>
-__device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k, int ones_local, int lane) {
-  for (int u = valid_k * 8 + lane; u < 128 * 8; u += 32) {
+__device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k, int end_k, int ones_local,
+                                                        int lane) {
+  for (int u = valid_k * 8 + lane; u < end_k * 8; u += 32) {
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) *reinterpret_cast<uint4*>(sA + c * 16384 + u * 16) = make_uint4(0, 0, 0, 0);
   }
@@ -354,6 +357,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Cfg = TileCfg<BN, CG, B_MN>;
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
   constexpr int KR = (RAGGED_K && F8) ? 128 : BK;  // ragged-K: token rows per stage
+  constexpr int KMMA = F8 ? 32 : 16;                // K rows (elements) of one MMA instruction
+  constexpr int kMmaPerStage = 4;                   // 128 bytes of K per stage / 32 bytes per instruction
+  static_assert(!RAGGED_K || KR / KMMA == kMmaPerStage, "ragged-K stage depth");
   static_assert(!(RAGGED_K && F8) || (CG == 1 && (BN == 128 || BN == 256)), "e4m3 weight gradient: single CTA");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int TM = BM * CG;   // rows of a tile
@@ -622,8 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             relay_bits ^= 1u << stage;
             ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), par, abort_flag));
             if (!ok) break;
-            const int valid_k = min(BK, ti.k_end - (ti.k_start + kb * BK));
-            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
+            const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, (valid_k + KMMA - 1) / KMMA * KMMA,
+                                                         ones_local, lane);
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(leader_addr(&patch_done[stage]));
@@ -641,11 +648,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
         }
         ptx::tc_fence_after();
+        int n_mma = kMmaPerStage;  // MMA instructions of this stage (each reads 32 bytes of every K-major row)
         if constexpr (RAGGED_K) {
+          // a partial last stage of a group: only the K rows up to the next instruction boundary are
+          // multiplied, so only those past the group end need zeroing
           const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-          if (valid_k < KR || ones_local >= 0) {
-            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, ones_local, lane);
-            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, ones_local, lane);
+          n_mma = (valid_k + KMMA - 1) / KMMA;
+          if (valid_k < n_mma * KMMA || ones_local >= 0) {
+            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
+            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -656,7 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t adesc = ptx::make_smem_desc_sw128(sA, a_lbo, 1024);
           const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < kMmaPerStage; ++kk) {
+            if (kk >= n_mma) break;
             // one instruction consumes 32 bytes of every K-major row: K = 16 bf16 or K = 32 e4m3
             if constexpr (CG == 2 && F8) {
               ptx::umma_f8_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
