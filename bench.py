@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--ep-unfused", action="store_true",
                     help="peer transport: separate push kernels for the combine and the dispatch gradient instead "
                          "of the GEMM scatter epilogues")
+    ap.add_argument("--ep-no-pipeline", action="store_true",
+                    help="peer transport: dispatch + up-projection in one piece instead of two expert halves")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel dispatch/combine: peer-memory pushes or NCCL all-to-all")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch._grouped_mm comparator")
@@ -179,7 +181,9 @@ def build_workload(args, rank, world, device):
     desc = (f"cfg4: GPT-OSS-120B experts E={E_total} H=I=2880, {tokens} tokens/rank top-4 {args.routing} routing, "
             f"expert parallel E/{world} per GPU, dispatch/combine by "
             + (("peer-memory pushes over NVLink" + ("" if args.ep_unfused else
-                                                     ", combine and dispatch gradient stored by the GEMM epilogues"))
+                                                     ", combine and dispatch gradient stored by the GEMM epilogues"
+                                                     + ("" if args.ep_no_pipeline else
+                                                        ", dispatch pipelined with the up-proj in two expert halves")))
                if args.transport == "peer" else "NCCL all-to-all")
             + (", dispatch gradient pushed under the up-proj wgrad" if args.ep_overlap else ""))
     return wl, desc, E_total, 0, tokens, topk, H, I, 1.1, False
@@ -673,7 +677,7 @@ def main():
         ep_parity = ep_parity_check(args, world, rank, device)
         torch.cuda.empty_cache()
         ffn = EPMoEFFN(E_total, H, I, group=None, device=device, seed=2, transport=args.transport,
-                       overlap=args.ep_overlap, fused=not args.ep_unfused)
+                       overlap=args.ep_overlap, fused=not args.ep_unfused, pipeline=not args.ep_no_pipeline)
         gx = torch.Generator(device=device).manual_seed(1 + rank)
         x = torch.randn(tokens, H, generator=gx, device=device).to(torch.bfloat16).requires_grad_(True)
         expert_idx = route_tokens(tokens, E_total, topk, args.routing, seed=100 + rank, device=device)

@@ -106,6 +106,7 @@ struct Params {
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
   int wgrad_direct_k;       // WGRAD: groups of at most this many tokens store dW without TMA (-1 = none)
+  int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
 };
 
 struct TileInfo {
@@ -246,7 +247,7 @@ __device__ void build_schedule(const Params& p, const SchedSmem& s, int lane) {
       s.seg_start[e] = (int)sp;
       s.seg_end[e] = (int)ep;
       if constexpr (!RAGGED_K) {
-        cnt = (int)((ep - sp + TM - 1) / TM) * p.n_tiles;
+        cnt = e < p.group_begin ? 0 : (int)((ep - sp + TM - 1) / TM) * p.n_tiles;
       } else {
         cnt = p.m_tiles * p.n_tiles;
       }
@@ -1299,6 +1300,9 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.aux_v8 = v8_ok(g.aux, g.ld_aux) ? 1 : 0;
   p.d_v8 = v8_ok(g.d, g.ldd) ? 1 : 0;
   p.d_rows = reinterpret_cast<const long long*>(g.d_row_ptrs);
+  if (g.group_begin < 0 || g.group_begin > g.num_groups || (ragged_k && g.group_begin != 0))
+    return MGF_ERR_INVALID_ARGUMENT;
+  p.group_begin = g.group_begin;
   if (scatter) p.d_v8 = (g.n % 16) == 0 ? 1 : 0;  // per-row address alignment is checked in the kernel
   p.d2_v8 = v8_ok(g.d2, g.ldd2) ? 1 : 0;
   p.alpha = g.swiglu_alpha;

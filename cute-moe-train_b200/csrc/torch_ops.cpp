@@ -87,7 +87,7 @@ int sm_carveout_for(const Tensor& t) {
 // Ragged-M launch: A [total_rows, k] row-major, B [E, k, n] (either major), D [total_rows, n].
 void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& offs, const Tensor* bias,
                      const Tensor& d, const Tensor* d2, const Tensor* aux, double alpha, double limit,
-                     bool store_aux, const char* what, bool bias_per_row = false) {
+                     bool store_aux, const char* what, bool bias_per_row = false, int64_t group_begin = 0) {
   const bool b_col_major = check_strides_transposed(b, "mat_b");
   mgf_gemm_desc g = base_desc();
   g.epilogue = epi;
@@ -120,6 +120,7 @@ void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& of
   g.swiglu_limit = static_cast<float>(limit);
   g.store_aux = store_aux ? 1 : 0;
   g.bias_per_row = bias_per_row ? 1 : 0;
+  g.group_begin = static_cast<int32_t>(group_begin);
   g.sm_carveout = sm_carveout_for(a);
   check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
 }
@@ -311,9 +312,9 @@ std::tuple<Tensor, Tensor> mm_swiglu_cuda(const Tensor& mat_a, const Tensor& mat
 // csrc/binding.cu:36-63 `_grouped_mm_swiglu_cuda(mat_a, mat_b, offs, bias, aux_out, swiglu_out, alpha,
 // limit, store_aux)`: the caller allocates swiglu_out [M, I] (and aux_out [M, 2I] when store_aux);
 // the launch writes them in place.
-void swiglu_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
-                      const std::optional<Tensor>& aux_out, const Tensor& swiglu_out, double alpha, double limit,
-                      bool store_aux) {
+void swiglu_range_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
+                            const std::optional<Tensor>& aux_out, const Tensor& swiglu_out, double alpha,
+                            double limit, bool store_aux, int64_t group_begin) {
   TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "grouped_mm_swiglu: inputs must be CUDA tensors");
   const c10::cuda::CUDAGuard guard(mat_a.device());
   TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 3, "grouped_mm_swiglu requires mat_a 2D and mat_b 3D (ragged-M path)");
@@ -338,8 +339,15 @@ void swiglu_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& of
   if (store_aux)
     TORCH_CHECK(aux_out->dim() == 2 && aux_out->size(0) == M && aux_out->size(1) == N && aux_out->stride(1) == 1,
                 "aux_out must be a row-major bf16 [M, 2*I]");
+  TORCH_CHECK(group_begin >= 0 && group_begin <= offs.size(0), "grouped_mm_swiglu: group_begin out of range");
   launch_ragged_m(MGF_EPI_SWIGLU, mat_a, mat_b, offs, &bias, store_aux ? *aux_out : swiglu_out, &swiglu_out, nullptr,
-                  alpha, limit, store_aux, "grouped_mm_swiglu");
+                  alpha, limit, store_aux, "grouped_mm_swiglu", false, group_begin);
+}
+
+void swiglu_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& bias,
+                      const std::optional<Tensor>& aux_out, const Tensor& swiglu_out, double alpha, double limit,
+                      bool store_aux) {
+  swiglu_range_into_cuda(mat_a, mat_b, offs, bias, aux_out, swiglu_out, alpha, limit, store_aux, 0);
 }
 
 // csrc/binding.cu:68-118 `_grouped_mm_swiglu_bwd_cuda(grad_output, down_w_t, offs, aux_packed,
@@ -835,6 +843,9 @@ TORCH_LIBRARY(grouped_mm, m) {
       "swiglu_into(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, Tensor(a!)? aux_out, Tensor(b!) swiglu_out,"
       " float swiglu_alpha, float swiglu_limit, bool store_aux) -> ()");
   m.def(
+      "swiglu_range_into(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, Tensor(a!)? aux_out,"
+      " Tensor(b!) swiglu_out, float swiglu_alpha, float swiglu_limit, bool store_aux, int group_begin) -> ()");
+  m.def(
       "swiglu_bwd_into(Tensor grad_output, Tensor down_w_t, Tensor offs, Tensor aux_packed,"
       " Tensor(a!) grad_gate_up_packed, float swiglu_alpha, float swiglu_limit) -> ()");
   m.def("mm_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor? bias) -> Tensor");
@@ -867,6 +878,7 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_swiglu", &mm_swiglu_cuda);
   m.impl("mm_swiglu_noaux", &mm_swiglu_noaux_cuda);
   m.impl("swiglu_into", &swiglu_into_cuda);
+  m.impl("swiglu_range_into", &swiglu_range_into_cuda);
   m.impl("swiglu_bwd_into", &swiglu_bwd_into_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);

@@ -39,7 +39,7 @@ class MgfGemmDesc(ctypes.Structure):  # include/moe_gemm.h: mgf_gemm_desc
                 ("sm_carveout", ctypes.c_int32), ("workspace", ctypes.c_void_p),
                 ("bias_per_row", ctypes.c_int32), ("ab_type", ctypes.c_int32),
                 ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p), ("scale_b_stride", ctypes.c_int64),
-                ("d_row_ptrs", ctypes.c_void_p)]
+                ("d_row_ptrs", ctypes.c_void_p), ("group_begin", ctypes.c_int32)]
 
 
 _lib.mgf_grouped_gemm_launch.argtypes = [ctypes.POINTER(MgfGemmDesc), ctypes.c_void_p]

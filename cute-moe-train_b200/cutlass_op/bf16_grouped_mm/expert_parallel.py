@@ -342,11 +342,16 @@ class PeerBuffers:
     def push(self, kind: int, src, src_idx, scale, n_dev, dst_rank, dst_row, target: str, dst_rows: int, n_max: int):
         """One push into every rank's `target` buffer followed, on the same stream, by the wait for all
         ranks' pushes of this round: afterwards this rank's own `target`-side data is complete."""
+        self.wait(self.push_async(kind, src, src_idx, scale, n_dev, dst_rank, dst_row, target, dst_rows, n_max))
+
+    def push_async(self, kind: int, src, src_idx, scale, n_dev, dst_rank, dst_row, target: str, dst_rows: int,
+                   n_max: int) -> int:
+        """The push of push() without the wait, on the current stream; returns its sequence number."""
         self.seq += 1
         torch.ops.grouped_mm.push_rows(src, src_idx, scale, n_dev, dst_rank, dst_row, self.bases[target], dst_rows,
                                        src.shape[1], n_max, self.bases["flags"], self.counters[kind:kind + 1],
                                        self.seq, self.rank)
-        self.wait(self.seq)
+        return self.seq
 
     def signal(self) -> int:
         """Signal, after the stream's earlier work (a scatter-epilogue GEMM that wrote rows into the
@@ -475,6 +480,51 @@ class _PeerCombine(torch.autograd.Function):
         return st.bufs.local["grows"].view(st.cap, g.shape[1]), grad_w, None
 
 
+def _pipelined_dispatch_up(x, w_up, b_up, st):
+    """Dispatch + up-projection in two halves of the local experts, so the second half's rows cross
+    NVLink while the first half's GEMM runs: push the copies bound for every owner's first e_local/2
+    experts (main stream), push the rest on the side stream, wait for the first push, run the
+    up-proj + bias + SwiGLU over experts [0, h), wait for the second push, run it over [h, e_local)
+    (mgf_gemm_desc.group_begin) into the same outputs."""
+    bufs, plan = st.bufs, st.plan
+    offs = plan["offs"]
+    el = offs.numel()
+    h = el // 2
+    n = st.n
+    with timed("ep_peer_dispatch"):
+        first = torch.remainder(st.e_sorted, el) < h
+        perm = torch.argsort((~first).to(torch.int8), stable=True)  # first-half copies, then the rest
+        n_a = first.sum(dtype=torch.int32).view(1)
+        n_b = (n - n_a).to(torch.int32)
+        src = st.copy_token[perm]
+        d_rank = plan["dst_rank"][perm]
+        d_row = plan["dst_row"][perm]
+        seq_a = bufs.push_async(0, x, src, None, n_a, d_rank, d_row, "rows", st.cap, n)
+        main = torch.cuda.current_stream()
+        side = bufs.side_stream
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            seq_b = bufs.push_async(1, x, src.flip(0), None, n_b, d_rank.flip(0), d_row.flip(0), "rows", st.cap, n)
+        for t in (src, d_rank, d_row, n_b):
+            t.record_stream(side)
+        bufs.wait(seq_a)
+    rows = bufs.local["rows"]
+    two_i = w_up.shape[2]
+    s = torch.empty_strided((st.cap, two_i // 2), (_padded_cols(two_i // 2), 1), dtype=rows.dtype, device=rows.device)
+    aux = torch.empty_strided((st.cap, two_i), (_padded_cols(two_i), 1), dtype=rows.dtype, device=rows.device)
+    with timed("up_swiglu_fwd"):
+        torch.ops.grouped_mm.swiglu_range_into(rows, w_up[:h], offs[:h], b_up[:h], aux, s, st.alpha, st.limit,
+                                               True, 0)
+        bufs.wait(seq_b)
+        torch.ops.grouped_mm.swiglu_range_into(rows, w_up, offs, b_up, aux, s, st.alpha, st.limit, True, h)
+    main.wait_stream(side)
+    return s, aux
+
+
+def _padded_cols(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
 class _PeerMoE(torch.autograd.Function):
     """The expert-parallel MoE FFN of the peer transport in one autograd function, with the combine
     and the dispatch gradient fused into GEMM epilogues.
@@ -494,12 +544,16 @@ class _PeerMoE(torch.autograd.Function):
     def forward(ctx, x, w_up, b_up, w_down, b_down, w_flat, st):
         bufs, plan = st.bufs, st.plan
         offs = plan["offs"]
-        with timed("ep_peer_dispatch"):
-            bufs.push(0, x.contiguous(), st.copy_token, None, None, plan["dst_rank"], plan["dst_row"], "rows",
-                      st.cap, st.n)
         rows = bufs.local["rows"]
-        with timed("up_swiglu_fwd"):
-            s, aux = torch.ops.grouped_mm.mm_swiglu(rows, w_up, offs, b_up, st.alpha, st.limit)
+        el = offs.numel()
+        if st.pipeline and el >= 2:
+            s, aux = _pipelined_dispatch_up(x.contiguous(), w_up, b_up, st)
+        else:
+            with timed("ep_peer_dispatch"):
+                bufs.push(0, x.contiguous(), st.copy_token, None, None, plan["dst_rank"], plan["dst_row"], "rows",
+                          st.cap, st.n)
+            with timed("up_swiglu_fwd"):
+                s, aux = torch.ops.grouped_mm.mm_swiglu(rows, w_up, offs, b_up, st.alpha, st.limit)
         with timed("down_fwd"):
             torch.ops.grouped_mm.mm_scatter(s, w_down, offs, b_down, plan["ptr_ret"])
         bufs.wait(bufs.signal())
@@ -578,7 +632,7 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
     st = _PeerState()
     with timed("ep_plan"):
         order, inv_order, copy_token, e_sorted, counts = torch.ops.grouped_mm.ep_sort(expert_idx, num_experts, k)
-        st.order, st.inv_order, st.copy_token = order, inv_order, copy_token
+        st.order, st.inv_order, st.copy_token, st.e_sorted = order, inv_order, copy_token, e_sorted
         c_all = torch.empty(world, num_experts, dtype=counts.dtype, device=x.device)
         # the count exchange also orders this call after every rank's previous use of the buffers
         dist.all_gather_into_tensor(c_all, counts, group=group)
@@ -592,6 +646,7 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
     st.overlap = overlap
     if fused is not None:
         st.alpha, st.limit = fused["alpha"], fused["limit"]
+        st.pipeline = fused.get("pipeline", True)
         w_flat = router_weights.reshape(-1).float().contiguous() if router_weights is not None else None
         out = _PeerMoE.apply(x, fused["w_up"], fused["b_up"], fused["w_down"], fused["b_down"], w_flat, st)
         bufs.pending_backward = out.requires_grad
@@ -614,16 +669,20 @@ class EPMoEFFN(torch.nn.Module):
 
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
                  swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer",
-                 overlap: bool = False, capacity_factor: float = 2.0, fused: bool = True):
+                 overlap: bool = False, capacity_factor: float = 2.0, fused: bool = True,
+                 pipeline: bool = True):
         """transport: "peer" (NVLink pushes, CUDA, world > 1) or "nccl" (all-to-all).  overlap (peer
         transport): push the dispatch's gradient on a side stream under the up-projection weight
         gradient instead of after it.  capacity_factor (peer transport): receive buffers hold
         ceil(capacity_factor * tokens * topk) rows per rank (overflow is reported, see
         ep_moe_ffn_peer).  fused (peer transport): the combine and the dispatch gradient are written by
         the down-proj forward / up-proj dgrad epilogues straight into the source ranks (_PeerMoE);
-        False: separate push kernels around the FFN (then `overlap` applies)."""
+        False: separate push kernels around the FFN (then `overlap` applies).  pipeline (fused peer
+        transport, at least 2 local experts): the dispatch and the up-projection run in two halves
+        of the local experts, the second half's push overlapping the first half's GEMM."""
         super().__init__()
         self.fused = fused
+        self.pipeline = pipeline
         self.overlap = overlap
         self.capacity_factor = capacity_factor
         if transport not in ("peer", "nccl"):
@@ -665,7 +724,7 @@ class EPMoEFFN(torch.nn.Module):
             fused = None
             if self.fused:
                 fused = {"w_up": self.w_up, "b_up": self.b_up, "w_down": self.w_down, "b_down": self.b_down,
-                         "alpha": self.alpha, "limit": self.limit}
+                         "alpha": self.alpha, "limit": self.limit, "pipeline": self.pipeline}
             out, st = ep_moe_ffn_peer(x, expert_idx, self.num_experts, self._peer_expert_fn, self._peer_bufs,
                                       self.group, router_weights, overlap=self.overlap,
                                       capacity_factor=self.capacity_factor, fused=fused)

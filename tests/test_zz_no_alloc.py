@@ -34,7 +34,7 @@ class MgfGemmDesc(ctypes.Structure):
                 ("swiglu_alpha", ctypes.c_float), ("swiglu_limit", ctypes.c_float), ("store_aux", ctypes.c_int32),
                 ("sm_carveout", ctypes.c_int32), ("workspace", ctypes.c_void_p), ("bias_per_row", ctypes.c_int32),
                 ("ab_type", ctypes.c_int32), ("scale_a", ctypes.c_void_p), ("scale_b", ctypes.c_void_p),
-                ("scale_b_stride", ctypes.c_int64), ("d_row_ptrs", ctypes.c_void_p)]
+                ("scale_b_stride", ctypes.c_int64), ("d_row_ptrs", ctypes.c_void_p), ("group_begin", ctypes.c_int32)]
 
 
 MGF_EPI_WGRAD = 3
