@@ -592,6 +592,45 @@ def extra_workloads(args, mgf, device, peaks, peak_src):
         except Exception as e:  # report, do not fail the bench
             out[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         torch.cuda.empty_cache()
+    # the cfg3 FFN with every forward and backward GEMM in e4m3 (quantisation inside the step), next to
+    # a measured cuBLAS e4m3 GEMM peak (torch._scaled_mm, 8192^3, best of 10) as its denominator
+    try:
+        from cutlass_op.bf16_grouped_mm import fp8 as fp8_mod
+
+        counts, M, offs, x, w_up, b_up, w_down, b_down = single_gpu_setup(
+            args, "cfg3", 32, 2, 24576, 4, 2880, 2880, 1.1, device)
+        params = [x, w_up, b_up, w_down, b_down]
+
+        def step():
+            for p_ in params:
+                p_.grad = None
+            fp8_mod.grouped_mm_ffn_fp8(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT).sum().backward()
+        for _ in range(warm):
+            step()
+        ms = time_steps(step, steps, 0)
+        del x, w_up, b_up, w_down, b_down, params, step
+        torch.cuda.empty_cache()
+        a = torch.randn(8192, 8192, device=device).to(torch.float8_e4m3fn)
+        b = torch.randn(8192, 8192, device=device).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=device)
+        best = 1e9
+        for _ in range(13):
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            ev1.record()
+            torch.cuda.synchronize()
+            best = min(best, ev0.elapsed_time(ev1))
+        peak8 = 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+        tf = 18.0 * M * 2880 * 2880 / (ms * 1e-3) / 1e12
+        out["cfg3_fp8_ffn"] = {"ms_per_step": ms, "tflops": tf, "measured_e4m3_peak_tflops": peak8,
+                               "frac_of_measured_e4m3_peak": tf / peak8,
+                               "what": "grouped_mm_ffn_fp8 fwd+bwd at cfg3 (every GEMM e4m3, bf16 in/out, "
+                                       "quantisers inside the step); peak = torch._scaled_mm e4m3 8192^3 burst"}
+        del a, b
+    except Exception as e:
+        out["cfg3_fp8_ffn"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    torch.cuda.empty_cache()
     try:
         from cutlass_op.bf16_grouped_mm.expert_parallel import EPMoEFFN, route_tokens
 
