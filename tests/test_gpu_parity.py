@@ -244,3 +244,29 @@ def test_rows_past_offs_end_are_never_written():
     for name, got in (("swiglu_out", s_out), ("aux", aux_out), ("grad_aux", g_packed.view(torch.bfloat16))):
         r = O.check(name, got[:rows].float().cpu(), ref[name][:rows])
         assert r["ok"], r
+
+
+def test_group_range_launches_equal_one_launch():
+    """Two launches over the expert ranges [0, h) and [h, E) of one offs array (group_begin), writing
+    into the same outputs, give the single launch's results bit for bit (single CTAs and pairs)."""
+    import os
+
+    _lib()
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    for cg in ("1", "2"):
+        os.environ["MGF_CTA_GROUP"] = cg
+        try:
+            x, w_up, b_up, _, _, offs, _ = small_case(6, 256, 128, [300, 0, 517, 41, 600, 1], seed=41)
+            x, w_up, b_up, offs = (t.cuda() for t in (x, w_up, b_up, offs))
+            s_ref, aux_ref = torch.ops.grouped_mm.mm_swiglu(x, w_up, offs, b_up, 1.702, 7.0)
+            M, I = x.shape[0], w_up.shape[2] // 2
+            s = torch.full((M, I), float("nan"), dtype=torch.bfloat16, device="cuda")
+            aux = torch.full((M, 2 * I), float("nan"), dtype=torch.bfloat16, device="cuda")
+            h = 3
+            torch.ops.grouped_mm.swiglu_range_into(x, w_up[:h], offs[:h], b_up[:h], aux, s, 1.702, 7.0, True, 0)
+            torch.ops.grouped_mm.swiglu_range_into(x, w_up, offs, b_up, aux, s, 1.702, 7.0, True, h)
+            torch.cuda.synchronize()
+            assert torch.equal(s, s_ref) and torch.equal(aux, aux_ref), cg
+        finally:
+            del os.environ["MGF_CTA_GROUP"]
