@@ -105,8 +105,8 @@ struct Params {
   int stall_test;     // test hook: the producer hands out no tiles, so every consumer wait runs out
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
-  int wgrad_direct_k;       // WGRAD: groups of at most this many tokens store dW without TMA (-1 = none)
   int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
+  int ktail_trim;           // ragged-K: a partial last stage multiplies only up to the next instruction boundary
 };
 
 struct TileInfo {
@@ -634,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), par, abort_flag));
             if (!ok) break;
             const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, (valid_k + KMMA - 1) / KMMA * KMMA,
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, p.ktail_trim ? (valid_k + KMMA - 1) / KMMA * KMMA : KR,
                                                          ones_local, lane);
             ptx::fence_proxy_async_smem();
             __syncwarp();
@@ -658,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // a partial last stage of a group: only the K rows up to the next instruction boundary are
           // multiplied, so only those past the group end need zeroing
           const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-          n_mma = (valid_k + KMMA - 1) / KMMA;
+          n_mma = p.ktail_trim ? (valid_k + KMMA - 1) / KMMA : kMmaPerStage;
           if (valid_k < n_mma * KMMA || ones_local >= 0) {
             if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
             else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
@@ -886,8 +886,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
         const bool row_bias = (r == ones_r);
         const bool warp_rows = m0 + q * 32 < p.m;  // this warp holds rows of dW
-        // groups of at most p.wgrad_direct_k tokens: direct global stores instead of TMA tile stores
-        const bool direct = ti.k_end - ti.k_start <= p.wgrad_direct_k;
         const bool warp_active = warp_rows || (ones_r >= q * 32 && ones_r < q * 32 + 32);
         uint8_t* slice = out_stage + (warp - 2) * (32 * 64);
         const uint32_t slice_u32 = ptx::smem_u32(slice);
@@ -921,18 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int h = 0; h < 16; ++h) packed[h] = 0u;
             }
-            if (warp_rows && direct) {
-              // short groups: every lane stores its own row's 64 bytes straight from registers (no
-              // staging, no wait on the previous store), rows past m and columns past n skipped
-              if (m0 + r < p.m) {
-                const uint4 u[4] = {make_uint4(packed[0], packed[1], packed[2], packed[3]),
-                                    make_uint4(packed[4], packed[5], packed[6], packed[7]),
-                                    make_uint4(packed[8], packed[9], packed[10], packed[11]),
-                                    make_uint4(packed[12], packed[13], packed[14], packed[15])};
-                store_units<4>(p.d + (int64_t)ti.e * p.ldd_batch + (int64_t)(m0 + r) * p.ldd + col0, u,
-                               (p.n - col0) >> 3, p.d_v8);
-              }
-            } else if (warp_rows) {
+            if (warp_rows) {
               if (lane == 0) ptx::bulk_wait_read_all();  // the slice's previous store has read it
               __syncwarp();
               // 64-byte swizzle (matches the tensor map): 16-byte unit g of row `lane` at g ^ ((lane >> 1) & 3)
@@ -1461,12 +1448,9 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // The dynamic tile counter serves single CTAs only: both CTAs of a pair must walk the same tile
   // sequence, which static striding gives them.
   p.tile_counter = (g.epilogue == MGF_EPI_WGRAD) ? g.workspace : nullptr;
-  p.wgrad_direct_k = -1;
-  if (ragged_k) {
-    const char* env = getenv("MGF_WGRAD_DIRECT_K");
-    p.wgrad_direct_k = env != nullptr ? atoi(env) : -1;
-    // 32-byte stores only where the dW base and its row and batch pitches keep them aligned
-    p.d_v8 = ((reinterpret_cast<uintptr_t>(g.d) & 31u) == 0 && (g.ldd % 16) == 0 && (g.ldd_batch % 16) == 0) ? 1 : 0;
+  {
+    const char* env = getenv("MGF_KTAIL_TRIM");  // 0: multiply whole stages (comparison runs)
+    p.ktail_trim = (env != nullptr && env[0] == '0') ? 0 : 1;
   }
   // Test hook for the bounded waits: with MGF_TEST_STALL_PRODUCER=1 the kernel does no work and
   // every consumer wait gives up after its limit, setting MGF_DEV_WAIT_TIMEOUT.  Nothing is in flight
