@@ -9,7 +9,11 @@ routed rows of 24576 tokens (top-4): useful FLOPs 18*M*H*I (M = routed rows on t
 
 N=1 runs config 3 (GPT-OSS-20B experts, E=32, H=I=2880, Zipf(1.1) top-4 routing with two experts
 receiving no tokens).  N>1 (torchrun) runs config 4 under expert parallelism (GPT-OSS-120B experts,
-E=128 split E/N per GPU, 24576 tokens per rank, NCCL all-to-all dispatch/combine), weak scaling.
+E=128 split E/N per GPU, 24576 tokens per rank, NVLink peer-memory dispatch/combine), weak scaling,
+after an expert-parallel parity self-check against the oracle (``ep_parity``).  At N=1 the line also
+carries secondary measurements (``extra``: cfg2 forward, cfg5 at 4096 tokens, the FP8 FFN, cfg4 on one
+GPU), the torch._grouped_mm comparator, the end-to-end leg and the CPU baseline.
+``--impl reference`` times the reference's own Python layer over a CPU restatement of its kernels.
 All inputs are seeded synthetic data of the configured shapes.  Rank 0 prints one JSON line.
 """
 

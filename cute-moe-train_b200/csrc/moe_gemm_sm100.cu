@@ -634,8 +634,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), par, abort_flag));
             if (!ok) break;
             const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, p.ktail_trim ? (valid_k + KMMA - 1) / KMMA * KMMA : KR,
-                                                         ones_local, lane);
+            const int end_k = p.ktail_trim ? (valid_k + KMMA - 1) / KMMA * KMMA : KR;
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(leader_addr(&patch_done[stage]));
