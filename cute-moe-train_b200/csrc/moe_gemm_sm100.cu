@@ -106,7 +106,6 @@ struct Params {
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
   int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
-  int ktail_trim;           // ragged-K: a partial last stage multiplies only up to the next instruction boundary
 };
 
 struct TileInfo {
@@ -634,8 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&full_bar[stage]), par, abort_flag));
             if (!ok) break;
             const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-            const int end_k = p.ktail_trim ? (valid_k + KMMA - 1) / KMMA * KMMA : KR;
-            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
+            patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, KR, ones_local, lane);
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive_cluster(leader_addr(&patch_done[stage]));
@@ -653,15 +651,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
         }
         ptx::tc_fence_after();
-        int n_mma = kMmaPerStage;  // MMA instructions of this stage (each reads 32 bytes of every K-major row)
         if constexpr (RAGGED_K) {
-          // a partial last stage of a group: only the K rows up to the next instruction boundary are
-          // multiplied, so only those past the group end need zeroing
           const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-          n_mma = p.ktail_trim ? (valid_k + KMMA - 1) / KMMA : kMmaPerStage;
-          if (valid_k < n_mma * KMMA || ones_local >= 0) {
-            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
-            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, n_mma * KMMA, ones_local, lane);
+          if (valid_k < KR || ones_local >= 0) {
+            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, KR, ones_local, lane);
+            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, KR, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -673,7 +667,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
 #pragma unroll
           for (int kk = 0; kk < kMmaPerStage; ++kk) {
-            if (kk >= n_mma) break;
             // one instruction consumes 32 bytes of every K-major row: K = 16 bf16 or K = 32 e4m3
             if constexpr (CG == 2 && F8) {
               ptx::umma_f8_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -1448,10 +1441,6 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   // The dynamic tile counter serves single CTAs only: both CTAs of a pair must walk the same tile
   // sequence, which static striding gives them.
   p.tile_counter = (g.epilogue == MGF_EPI_WGRAD) ? g.workspace : nullptr;
-  {
-    const char* env = getenv("MGF_KTAIL_TRIM");  // 0: multiply whole stages (comparison runs)
-    p.ktail_trim = (env != nullptr && env[0] == '0') ? 0 : 1;
-  }
   // Test hook for the bounded waits: with MGF_TEST_STALL_PRODUCER=1 the kernel does no work and
   // every consumer wait gives up after its limit, setting MGF_DEV_WAIT_TIMEOUT.  Nothing is in flight
   // when they give up, so the context stays usable; tests use it to exercise that path on a GPU.
