@@ -1,0 +1,231 @@
+// e4m3 quantisers of the FP8 MoE FFN: bf16 -> float8_e4m3fn with fp32 scales, scale = amax / 448
+// (max(amax, 1e-12)), q = saturate_to_e4m3(x / scale), round to nearest even.
+//
+//   rows     one scale per row of a [rows, cols] matrix (the ragged-M A operands): one warp per row,
+//            16-byte loads, the row read twice (amax, then quantise; the second pass hits L1/L2);
+//   cols     one scale per column (the ragged-K weight-gradient operands): per-column amax by an
+//            atomicMax on the fp32 bit patterns of |x| (non-negative floats order like their bits),
+//            then an elementwise pass;
+//   weights  [E, K, N] (any strides) -> e4m3 [E, N, K] with K contiguous (the K-major B operand) and
+//            one scale per (e, n): the same two passes over 32 x 32 tiles, the second transposing
+//            through shared memory so that both the read and the write are coalesced.
+// These replace chains of eager torch ops (abs, amax, divide, clamp, copy, transpose) that cost more
+// than the e4m3 GEMMs they feed.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "moe_gemm.h"
+
+namespace mgf {
+namespace {
+
+constexpr float kE4M3Max = 448.0f;
+
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ float scale_of(float amax) { return fmaxf(amax, 1e-12f) / kE4M3Max; }
+
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                         int64_t cols, int64_t ldx, uint8_t* __restrict__ q,
+                                                         int64_t ldq, float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + row * ldx;
+  const int64_t nv = cols / 8;  // whole 16-byte vectors; cols % 8 == 0 is checked by the host
+  float amax = 0.0f;
+  for (int64_t v = lane; v < nv; v += 32) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + v);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float s = scale_of(amax);
+  if (lane == 0) scale[row] = s;
+  uint8_t* qr = q + row * ldq;
+  for (int64_t v = lane; v < nv; v += 32) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(xr) + v);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float2 a = __bfloat1622float2(h[2 * j]);
+      const float2 b = __bfloat1622float2(h[2 * j + 1]);
+      w[j] = static_cast<uint32_t>(to_e4m3(a.x / s)) | (static_cast<uint32_t>(to_e4m3(a.y / s)) << 8) |
+             (static_cast<uint32_t>(to_e4m3(b.x / s)) << 16) | (static_cast<uint32_t>(to_e4m3(b.y / s)) << 24);
+    }
+    *reinterpret_cast<uint2*>(qr + v * 8) = make_uint2(w[0], w[1]);
+  }
+}
+
+// column amax: a block covers 8 * 32 columns (one 16-byte vector per thread) and kRowsPerBlock rows
+constexpr int kRowsPerBlock = 64;
+
+__global__ void __launch_bounds__(256) col_amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                       int64_t cols, int64_t ldx, unsigned int* __restrict__ amax) {
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * 32 + (threadIdx.x & 31);  // vector index along cols
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRowsPerBlock + (threadIdx.x >> 5);
+  if (v * 8 >= cols) return;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int64_t r = r0; r < rows && r < (static_cast<int64_t>(blockIdx.y) + 1) * kRowsPerBlock; r += 8) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+      m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) atomicMax(amax + v * 8 + j, __float_as_uint(m[j]));
+}
+
+__global__ void amax_to_scale_kernel(float* __restrict__ s, int64_t n) {  // in place: amax bits -> scale
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) s[i] = scale_of(__uint_as_float(reinterpret_cast<unsigned int*>(s)[i]));
+}
+
+__global__ void __launch_bounds__(256) quant_cols_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                         int64_t cols, int64_t ldx, const float* __restrict__ scale,
+                                                         uint8_t* __restrict__ q, int64_t ldq) {
+  const int64_t nv = cols / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * nv) return;
+  const int64_t r = i / nv, v = i - r * nv;
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + v * 8));
+  const float4 s1 = __ldg(reinterpret_cast<const float4*>(scale + v * 8) + 1);
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  uint32_t w[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float2 a = __bfloat1622float2(h[2 * j]);
+    const float2 b = __bfloat1622float2(h[2 * j + 1]);
+    w[j] = static_cast<uint32_t>(to_e4m3(a.x / sv[4 * j])) | (static_cast<uint32_t>(to_e4m3(a.y / sv[4 * j + 1])) << 8) |
+           (static_cast<uint32_t>(to_e4m3(b.x / sv[4 * j + 2])) << 16) |
+           (static_cast<uint32_t>(to_e4m3(b.y / sv[4 * j + 3])) << 24);
+  }
+  *reinterpret_cast<uint2*>(q + r * ldq + v * 8) = make_uint2(w[0], w[1]);
+}
+
+// Weights: tile of 32 (k) x 32 (n) of expert blockIdx.z; N_FAST: the input's unit stride is along n
+// (threadIdx.x walks n), else along k.
+template <bool N_FAST>
+__global__ void __launch_bounds__(256) w_amax_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                     int64_t s_e, int64_t s_k, int64_t s_n,
+                                                     unsigned int* __restrict__ amax) {
+  __shared__ float tile[32][33];
+  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 32, n0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t k = k0 + (N_FAST ? j : tx), n = n0 + (N_FAST ? tx : j);
+    float v = 0.0f;
+    if (k < K && n < N) v = fabsf(__bfloat162float(w[e * s_e + k * s_k + n * s_n]));
+    if (N_FAST) tile[j][tx] = v; else tile[tx][j] = v;  // tile[k][n]
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = 0.0f;
+    for (int k = 0; k < 32; ++k) m = fmaxf(m, tile[k][threadIdx.x]);
+    const int64_t n = n0 + threadIdx.x;
+    if (n < N) atomicMax(amax + e * N + n, __float_as_uint(m));
+  }
+}
+
+template <bool N_FAST>
+__global__ void __launch_bounds__(256) w_quant_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                      int64_t s_e, int64_t s_k, int64_t s_n,
+                                                      const float* __restrict__ scale, uint8_t* __restrict__ q,
+                                                      int64_t ldq) {
+  __shared__ float tile[32][33];
+  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 32, n0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t k = k0 + (N_FAST ? j : tx), n = n0 + (N_FAST ? tx : j);
+    float v = 0.0f;
+    if (k < K && n < N) v = __bfloat162float(w[e * s_e + k * s_k + n * s_n]);
+    if (N_FAST) tile[j][tx] = v; else tile[tx][j] = v;
+  }
+  __syncthreads();
+  // output q[e][n][k], k contiguous: threadIdx.x walks k
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t n = n0 + j, k = k0 + tx;
+    if (n < N && k < K) q[(e * N + n) * ldq + k] = to_e4m3(tile[tx][j] / __ldg(scale + e * N + n));
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace mgf
+
+extern "C" int mgf_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq,
+                                     float* scale, void* stream) {
+  using namespace mgf;
+  if (rows < 0 || cols < 0 || (rows > 0 && (x == nullptr || q == nullptr || scale == nullptr)))
+    return MGF_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return MGF_OK;
+  if (cols % 8 || ldx % 8 || ldq % 8 || !aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return MGF_ERR_ALIGNMENT;
+  const int64_t blocks = (rows * 32 + 255) / 256;
+  quant_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), rows, cols, ldx, static_cast<uint8_t*>(q), ldq, scale);
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_fp8_quantize_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq,
+                                     float* scale, void* stream) {
+  using namespace mgf;
+  if (rows < 0 || cols < 0 || (cols > 0 && scale == nullptr) || (rows > 0 && (x == nullptr || q == nullptr)))
+    return MGF_ERR_INVALID_ARGUMENT;
+  if (cols == 0) return MGF_OK;
+  if (cols % 8 || ldx % 8 || ldq % 8 || !aligned16(x) || !aligned16(scale) || (reinterpret_cast<uintptr_t>(q) & 7u))
+    return MGF_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scale, 0, sizeof(float) * cols, st) != cudaSuccess) return MGF_ERR_CUDA;
+  if (rows > 0) {
+    const dim3 grid(static_cast<unsigned>((cols / 8 + 31) / 32), static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock));
+    col_amax_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, ldx,
+                                          reinterpret_cast<unsigned int*>(scale));
+  }
+  amax_to_scale_kernel<<<static_cast<unsigned>((cols + 255) / 256), 256, 0, st>>>(scale, cols);
+  if (rows > 0) {
+    const int64_t items = rows * (cols / 8);
+    quant_cols_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), rows, cols, ldx, scale, static_cast<uint8_t*>(q), ldq);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k,
+                                        int64_t s_n, void* q, int64_t ldq, float* scale, void* stream) {
+  using namespace mgf;
+  if (E < 0 || K < 0 || N < 0 || ldq < K) return MGF_ERR_INVALID_ARGUMENT;
+  if (E == 0 || N == 0) return MGF_OK;
+  if (w == nullptr || q == nullptr || scale == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scale, 0, sizeof(float) * E * N, st) != cudaSuccess) return MGF_ERR_CUDA;
+  const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
+  const bool n_fast = s_n == 1;
+  const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(w);
+  if (K > 0) {
+    if (n_fast) w_amax_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, reinterpret_cast<unsigned int*>(scale));
+    else w_amax_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, reinterpret_cast<unsigned int*>(scale));
+  }
+  amax_to_scale_kernel<<<static_cast<unsigned>((E * N + 255) / 256), 256, 0, st>>>(scale, E * N);
+  if (K > 0) {
+    if (n_fast) w_quant_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+    else w_quant_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}

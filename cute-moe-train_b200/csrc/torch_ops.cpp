@@ -811,6 +811,48 @@ std::vector<Tensor> ep_routes_cuda(const Tensor& c_all_in, const Tensor& e_sorte
           ptr_ret.defined() ? ptr_ret : at::empty({0}, opt), ptr_gret.defined() ? ptr_gret : at::empty({0}, opt)};
 }
 
+// ---------------------------------------------------------------- e4m3 quantisers
+int64_t pad16(int64_t n) { return (n + 15) / 16 * 16; }
+
+std::tuple<Tensor, Tensor> fp8_quantize_rows_cuda(const Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1,
+              "fp8_quantize_rows: x must be a row-major bf16 [rows, cols] CUDA tensor");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = x.size(0), cols = x.size(1);
+  Tensor q = at::empty_strided({rows, cols}, {pad16(cols), 1}, x.options().dtype(at::kFloat8_e4m3fn));
+  Tensor scale = at::empty({rows}, x.options().dtype(at::kFloat));
+  check_launch(mgf_fp8_quantize_rows(x.data_ptr(), rows, cols, x.stride(0), q.data_ptr(), q.stride(0),
+                                     scale.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()),
+               "fp8_quantize_rows");
+  return {q, scale};
+}
+
+std::tuple<Tensor, Tensor> fp8_quantize_cols_cuda(const Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1,
+              "fp8_quantize_cols: x must be a row-major bf16 [rows, cols] CUDA tensor");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = x.size(0), cols = x.size(1);
+  Tensor q = at::empty_strided({rows, cols}, {pad16(cols), 1}, x.options().dtype(at::kFloat8_e4m3fn));
+  Tensor scale = at::empty({cols}, x.options().dtype(at::kFloat));
+  check_launch(mgf_fp8_quantize_cols(x.data_ptr(), rows, cols, rows > 0 ? x.stride(0) : 8, q.data_ptr(), q.stride(0),
+                                     scale.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()),
+               "fp8_quantize_cols");
+  return {q, scale};
+}
+
+std::tuple<Tensor, Tensor> fp8_quantize_weights_cuda(const Tensor& w) {
+  TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == at::kBFloat16 && (w.stride(2) == 1 || w.stride(1) == 1),
+              "fp8_quantize_weights: w must be a bf16 [E, K, N] CUDA tensor with unit stride along K or N");
+  const c10::cuda::CUDAGuard guard(w.device());
+  const int64_t E = w.size(0), K = w.size(1), N = w.size(2), kp = pad16(K);
+  Tensor qt = at::empty({E, N, kp}, w.options().dtype(at::kFloat8_e4m3fn));
+  Tensor scale = at::empty({E, N}, w.options().dtype(at::kFloat));
+  check_launch(mgf_fp8_quantize_weights(w.data_ptr(), E, K, N, w.stride(0), w.stride(1), w.stride(2), qt.data_ptr(),
+                                        kp, scale.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()),
+               "fp8_quantize_weights");
+  return {qt.as_strided({E, K, N}, {N * kp, 1, kp}), scale};
+}
+
 // Wait on the current stream until every slot of this rank's flag array reaches seq (see mgf_wait_flags).
 void wait_flags_cuda(const Tensor& flags, int64_t seq, int64_t timeout_ns) {
   TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kLong && flags.is_contiguous(),
@@ -865,6 +907,9 @@ TORCH_LIBRARY(grouped_mm, m) {
       " Tensor peer_bases, int dst_rows, int ld_dst, int n_max, Tensor? flag_bases=None, Tensor? counter=None,"
       " int seq=0, int rank=0) -> ()");
   m.def("wait_flags(Tensor flags, int seq, int timeout_ns) -> ()");
+  m.def("fp8_quantize_rows(Tensor x) -> (Tensor, Tensor)");
+  m.def("fp8_quantize_cols(Tensor x) -> (Tensor, Tensor)");
+  m.def("fp8_quantize_weights(Tensor w) -> (Tensor, Tensor)");
   m.def("signal_flags(Tensor flag_bases, int rank, int seq) -> ()");
   m.def("mm_scatter(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor row_ptrs) -> ()");
   m.def("ep_sort(Tensor expert_ids, int num_experts, int topk) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
@@ -890,6 +935,9 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("combine_rows", &combine_rows_cuda);
   m.impl("push_rows", &push_rows_cuda);
   m.impl("wait_flags", &wait_flags_cuda);
+  m.impl("fp8_quantize_rows", &fp8_quantize_rows_cuda);
+  m.impl("fp8_quantize_cols", &fp8_quantize_cols_cuda);
+  m.impl("fp8_quantize_weights", &fp8_quantize_weights_cuda);
   m.impl("signal_flags", &signal_flags_cuda);
   m.impl("mm_scatter", &mm_scatter_cuda);
   m.impl("ep_sort", &ep_sort_cuda);

@@ -67,8 +67,16 @@ def _mm_swiglu_fp8_fake(mat_a, mat_b, offs, scale_a, scale_b, bias, swiglu_alpha
     return s, aux
 
 
-def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [M] scales): x ~= q * scale[:, None]."""
+def _native(x: torch.Tensor) -> bool:
+    return x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0
+
+
+def quantize_rows(x: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [M] scales): x ~= q * scale[:, None].
+    bf16 CUDA inputs go through the fused kernel (grouped_mm::fp8_quantize_rows); the torch expression
+    below is the same formula (used for other dtypes, and by the tests as the reference)."""
+    if native and _native(x) and x.stride(-1) == 1:
+        return torch.ops.grouped_mm.fp8_quantize_rows(x.detach())
     amax = x.detach().abs().amax(dim=1).float().clamp_min(1e-12)
     scale = amax / E4M3_MAX
     k = x.shape[1]
@@ -78,9 +86,11 @@ def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, scale.contiguous()
 
 
-def quantize_weights(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+def quantize_weights(w: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """[E, K, N] -> (e4m3 [E, K, N] view with unit stride along K, fp32 [E, N] scales):
     w[e, :, n] ~= q[e, :, n] * scale[e, n]."""
+    if native and w.is_cuda and w.dtype == torch.bfloat16 and (w.stride(2) == 1 or w.stride(1) == 1):
+        return torch.ops.grouped_mm.fp8_quantize_weights(w.detach())
     amax = w.detach().abs().amax(dim=1).float().clamp_min(1e-12)  # [E, N]
     scale = amax / E4M3_MAX
     e, k, n = w.shape
@@ -90,11 +100,13 @@ def quantize_weights(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return qt.transpose(1, 2), scale.contiguous()
 
 
-def quantize_cols(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+def quantize_cols(x: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [K] scales): x ~= q * scale[None, :]
     (one scale per feature column over all rows: the weight-gradient operands)."""
-    amax = x.detach().abs().amax(dim=0).float().clamp_min(1e-12) if x.shape[0] else \
-        torch.ones(x.shape[1], device=x.device)
+    if native and _native(x) and x.stride(-1) == 1:
+        return torch.ops.grouped_mm.fp8_quantize_cols(x.detach())
+    amax = (x.detach().abs().amax(dim=0).float() if x.shape[0] else
+            torch.zeros(x.shape[1], device=x.device)).clamp_min(1e-12)
     scale = amax / E4M3_MAX
     k = x.shape[1]
     kp = (k + 15) // 16 * 16

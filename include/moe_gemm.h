@@ -223,6 +223,20 @@ int mgf_ep_routes(const int64_t* c_all, int32_t world, int32_t num_experts, cons
                   int64_t* dst_row, int64_t* src_rank, int64_t* src_pos, int64_t* ptr_ret, int64_t* ptr_gret,
                   int32_t* offs, int32_t* n_recv, void* stream);
 
+/* e4m3 quantisers of the FP8 path (no counterpart in the reference, which has no FP8): bf16 in,
+ * float8_e4m3fn out, fp32 scales = max(amax, 1e-12) / 448, q = saturate(x / scale), round to nearest.
+ *   rows:    x [rows, cols] (row stride ldx) -> q [rows, cols] (row stride ldq), scale [rows];
+ *   cols:    the same with one scale per column, scale [cols];
+ *   weights: w [E, K, N] with element strides s_e, s_k, s_n (s_n == 1 or s_k == 1 read coalesced)
+ *            -> q [E, N, K] with K contiguous (row stride ldq >= K), scale [E, N].
+ * cols, ldx and ldq multiples of 8, x 16-byte aligned.  Each a few kernels on `stream`, no host sync. */
+int mgf_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq, float* scale,
+                          void* stream);
+int mgf_fp8_quantize_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq, float* scale,
+                          void* stream);
+int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k, int64_t s_n,
+                             void* q, int64_t ldq, float* scale, void* stream);
+
 /* Map a peer process's device allocation (its 64-byte cudaIpcMemHandle_t) into the context of
  * the calling thread's current device, peer access enabled, for mgf_push_rows destinations
  * (no counterpart in the reference).  mgf_ipc_close unmaps it. */

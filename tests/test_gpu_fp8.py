@@ -152,3 +152,25 @@ def test_fp8_ffn_tracks_the_bf16_oracle():
         assert r["ok"], r
     for k in ("dw_up", "db_up", "dw_down", "db_down"):
         assert torch.count_nonzero(got[k][1]) == 0
+
+
+@pytest.mark.parametrize("shape", [(1029, 2880), (7, 64), (0, 128), (640, 5760)])
+def test_fused_quantisers_match_the_formula(shape):
+    """The fused e4m3 quantisers (rows, columns, weights in both layouts) give the torch formula's
+    scales and codes bit for bit on bf16 inputs."""
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(*shape, generator=g) * torch.linspace(0.01, 30.0, shape[1])).to(torch.bfloat16).cuda()
+    for fn in (fp8.quantize_rows, fp8.quantize_cols):
+        q, s = fn(x)
+        qr, sr = fn(x, native=False)
+        assert torch.equal(s, sr), fn.__name__
+        assert torch.equal(q.view(torch.uint8), qr.view(torch.uint8)), fn.__name__
+    if shape[0]:
+        w = x[: min(shape[0], 256)].reshape(1, -1, shape[1]).repeat(3, 1, 1)
+        for ww in (w, w.transpose(1, 2).contiguous().transpose(1, 2), w.transpose(1, 2)):
+            q, s = fp8.quantize_weights(ww)
+            qr, sr = fp8.quantize_weights(ww, native=False)
+            assert torch.equal(s, sr)
+            assert q.stride(1) == 1 and torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
