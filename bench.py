@@ -611,7 +611,11 @@ def extra_workloads(args, mgf, device, peaks, peak_src):
             fp8_mod.grouped_mm_ffn_fp8(x, w_up, w_down, offs, b_up, b_down, ALPHA, LIMIT).sum().backward()
         for _ in range(warm):
             step()
+        timer = OpTimer().install()
         ms = time_steps(step, steps, 0)
+        timer.uninstall()
+        fp8_ops = {k: round(v["avg_ms"], 4) for k, v in timer.summary().items()}
+        fp8_launches = {k: v["launches"] // steps for k, v in timer.summary().items()}
         del x, w_up, b_up, w_down, b_down, params, step
         torch.cuda.empty_cache()
         a = torch.randn(8192, 8192, device=device).to(torch.float8_e4m3fn)
@@ -628,6 +632,7 @@ def extra_workloads(args, mgf, device, peaks, peak_src):
         peak8 = 2 * 8192 ** 3 / (best * 1e-3) / 1e12
         tf = 18.0 * M * 2880 * 2880 / (ms * 1e-3) / 1e12
         out["cfg3_fp8_ffn"] = {"ms_per_step": ms, "tflops": tf, "measured_e4m3_peak_tflops": peak8,
+                               "ops_avg_ms": fp8_ops, "ops_per_step": fp8_launches,
                                "frac_of_measured_e4m3_peak": tf / peak8,
                                "what": "grouped_mm_ffn_fp8 fwd+bwd at cfg3 (every GEMM e4m3, bf16 in/out, "
                                        "quantisers inside the step); peak = torch._scaled_mm e4m3 8192^3 burst"}

@@ -76,9 +76,10 @@ def quantize_rows(x: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, t
     bf16 CUDA inputs go through the fused kernel (grouped_mm::fp8_quantize_rows); the torch expression
     below is the same formula (used for other dtypes, and by the tests as the reference)."""
     if native and _native(x) and x.stride(-1) == 1:
-        return torch.ops.grouped_mm.fp8_quantize_rows(x.detach())
+        with timed("fp8_quantize"):
+            return torch.ops.grouped_mm.fp8_quantize_rows(x.detach())
     amax = x.detach().abs().amax(dim=1).float().clamp_min(1e-12)
-    scale = amax / E4M3_MAX
+    scale = amax / torch.full_like(amax, E4M3_MAX)  # true division, as the kernels
     k = x.shape[1]
     kp = (k + 15) // 16 * 16
     q = torch.empty_strided((x.shape[0], k), (kp, 1), dtype=torch.float8_e4m3fn, device=x.device)
@@ -90,9 +91,10 @@ def quantize_weights(w: torch.Tensor, native: bool = True) -> tuple[torch.Tensor
     """[E, K, N] -> (e4m3 [E, K, N] view with unit stride along K, fp32 [E, N] scales):
     w[e, :, n] ~= q[e, :, n] * scale[e, n]."""
     if native and w.is_cuda and w.dtype == torch.bfloat16 and (w.stride(2) == 1 or w.stride(1) == 1):
-        return torch.ops.grouped_mm.fp8_quantize_weights(w.detach())
+        with timed("fp8_quantize"):
+            return torch.ops.grouped_mm.fp8_quantize_weights(w.detach())
     amax = w.detach().abs().amax(dim=1).float().clamp_min(1e-12)  # [E, N]
-    scale = amax / E4M3_MAX
+    scale = amax / torch.full_like(amax, E4M3_MAX)  # true division, as the kernels
     e, k, n = w.shape
     kp = (k + 15) // 16 * 16
     qt = torch.zeros((e, n, kp), dtype=torch.float8_e4m3fn, device=w.device)[:, :, :k]  # [E, N, K]
@@ -104,10 +106,11 @@ def quantize_cols(x: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, t
     """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [K] scales): x ~= q * scale[None, :]
     (one scale per feature column over all rows: the weight-gradient operands)."""
     if native and _native(x) and x.stride(-1) == 1:
-        return torch.ops.grouped_mm.fp8_quantize_cols(x.detach())
+        with timed("fp8_quantize"):
+            return torch.ops.grouped_mm.fp8_quantize_cols(x.detach())
     amax = (x.detach().abs().amax(dim=0).float() if x.shape[0] else
             torch.zeros(x.shape[1], device=x.device)).clamp_min(1e-12)
-    scale = amax / E4M3_MAX
+    scale = amax / torch.full_like(amax, E4M3_MAX)  # true division, as the kernels
     k = x.shape[1]
     kp = (k + 15) // 16 * 16
     q = torch.empty_strided((x.shape[0], k), (kp, 1), dtype=torch.float8_e4m3fn, device=x.device)
