@@ -67,27 +67,39 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
   }
 }
 
-// column amax: a block covers 8 * 32 columns (one 16-byte vector per thread) and kRowsPerBlock rows
-constexpr int kRowsPerBlock = 64;
+// column amax: a block covers 8 * 32 columns (one 16-byte vector per thread) and kRowsPerBlock rows;
+// the eight row lanes are reduced in shared memory, then one atomicMax per column and block
+constexpr int kRowsPerBlock = 1024;
 
 __global__ void __launch_bounds__(256) col_amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
                                                        int64_t cols, int64_t ldx, unsigned int* __restrict__ amax) {
-  const int64_t v = static_cast<int64_t>(blockIdx.x) * 32 + (threadIdx.x & 31);  // vector index along cols
-  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRowsPerBlock + (threadIdx.x >> 5);
-  if (v * 8 >= cols) return;
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * 32 + lane;  // vector index along cols
+  const int64_t r_begin = static_cast<int64_t>(blockIdx.y) * kRowsPerBlock;
+  const int64_t r_end = r_begin + kRowsPerBlock < rows ? r_begin + kRowsPerBlock : rows;
   float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int64_t r = r0; r < rows && r < (static_cast<int64_t>(blockIdx.y) + 1) * kRowsPerBlock; r += 8) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  if (v * 8 < cols) {
+    for (int64_t r = r_begin + ty; r < r_end; r += 8) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(h[j]);
-      m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
-      m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+        m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+      }
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) atomicMax(amax + v * 8 + j, __float_as_uint(m[j]));
+  for (int j = 0; j < 8; ++j) red[ty][lane * 8 + j] = m[j];
+  __syncthreads();
+  const int c = threadIdx.x;  // column within the block
+  float mm = red[0][c];
+#pragma unroll
+  for (int t = 1; t < 8; ++t) mm = fmaxf(mm, red[t][c]);
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * 256 + c;
+  if (col < cols) atomicMax(amax + col, __float_as_uint(mm));
 }
 
 __global__ void amax_to_scale_kernel(float* __restrict__ s, int64_t n) {  // in place: amax bits -> scale
@@ -119,27 +131,39 @@ __global__ void __launch_bounds__(256) quant_cols_kernel(const __nv_bfloat16* __
   *reinterpret_cast<uint2*>(q + r * ldq + v * 8) = make_uint2(w[0], w[1]);
 }
 
-// Weights: tile of 32 (k) x 32 (n) of expert blockIdx.z; N_FAST: the input's unit stride is along n
-// (threadIdx.x walks n), else along k.
+// Weights, per-(e, n) amax over k: one block per expert and strip of 32 columns, no atomics.
+// N_FAST: the input's unit stride is along n (lanes walk n, the 8 warps split k); else along k
+// (each warp takes 4 of the 32 columns, its lanes walk k).  Writes the scale directly.
 template <bool N_FAST>
 __global__ void __launch_bounds__(256) w_amax_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
                                                      int64_t s_e, int64_t s_k, int64_t s_n,
-                                                     unsigned int* __restrict__ amax) {
-  __shared__ float tile[32][33];
-  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 32, n0 = static_cast<int64_t>(blockIdx.x) * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
-  for (int j = ty; j < 32; j += 8) {
-    const int64_t k = k0 + (N_FAST ? j : tx), n = n0 + (N_FAST ? tx : j);
-    float v = 0.0f;
-    if (k < K && n < N) v = fabsf(__bfloat162float(w[e * s_e + k * s_k + n * s_n]));
-    if (N_FAST) tile[j][tx] = v; else tile[tx][j] = v;  // tile[k][n]
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) {
+                                                     float* __restrict__ scale) {
+  __shared__ float red[8][32];
+  const int64_t e = blockIdx.y, n0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const __nv_bfloat16* we = w + e * s_e;
+  if (N_FAST) {
+    const int64_t n = n0 + lane;
     float m = 0.0f;
-    for (int k = 0; k < 32; ++k) m = fmaxf(m, tile[k][threadIdx.x]);
-    const int64_t n = n0 + threadIdx.x;
-    if (n < N) atomicMax(amax + e * N + n, __float_as_uint(m));
+    if (n < N)
+      for (int64_t k = wid; k < K; k += 8) m = fmaxf(m, fabsf(__bfloat162float(we[k * s_k + n * s_n])));
+    red[wid][lane] = m;
+    __syncthreads();
+    if (wid == 0) {
+#pragma unroll
+      for (int t = 1; t < 8; ++t) m = fmaxf(m, red[t][lane]);
+      if (n < N) scale[e * N + n] = scale_of(m);
+    }
+  } else {
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = n0 + wid * 4 + j;
+      if (n >= N) break;
+      float m = 0.0f;
+      for (int64_t k = lane; k < K; k += 32) m = fmaxf(m, fabsf(__bfloat162float(we[k * s_k + n * s_n])));
+#pragma unroll
+      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if (lane == 0) scale[e * N + n] = scale_of(m);
+    }
   }
 }
 
@@ -214,16 +238,13 @@ extern "C" int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int
   if (E == 0 || N == 0) return MGF_OK;
   if (w == nullptr || q == nullptr || scale == nullptr) return MGF_ERR_INVALID_ARGUMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(scale, 0, sizeof(float) * E * N, st) != cudaSuccess) return MGF_ERR_CUDA;
-  const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
   const bool n_fast = s_n == 1;
   const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(w);
+  const dim3 agrid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>(E));
+  if (n_fast) w_amax_kernel<true><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
+  else w_amax_kernel<false><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
   if (K > 0) {
-    if (n_fast) w_amax_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, reinterpret_cast<unsigned int*>(scale));
-    else w_amax_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, reinterpret_cast<unsigned int*>(scale));
-  }
-  amax_to_scale_kernel<<<static_cast<unsigned>((E * N + 255) / 256), 256, 0, st>>>(scale, E * N);
-  if (K > 0) {
+    const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
     if (n_fast) w_quant_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
     else w_quant_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
   }
