@@ -189,6 +189,114 @@ __global__ void __launch_bounds__(256) w_quant_kernel(const __nv_bfloat16* __res
   }
 }
 
+// Vectorised weight kernels (16-byte loads along the contiguous dimension, 16-byte code stores along
+// k); used when the contiguous extent and the other strides are multiples of 8 elements and the base is
+// 16-byte aligned, which is the case for every weight layout of the FFN.
+template <bool N_FAST>
+__global__ void __launch_bounds__(256) w_amax_vec_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                         int64_t s_e, int64_t s_k, int64_t s_n,
+                                                         float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t e = blockIdx.y;
+  const __nv_bfloat16* we = w + e * s_e;
+  if (N_FAST) {  // a block: 256 columns (8 per lane), the 8 warps split k
+    __shared__ float red[8][256];
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 256 + lane * 8;
+    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (n0 < N) {
+      for (int64_t k = wid; k < K; k += 8) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(we + k * s_k + n0));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+          m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[wid][lane * 8 + j] = m[j];
+    __syncthreads();
+    float mm = red[0][threadIdx.x];
+#pragma unroll
+    for (int t = 1; t < 8; ++t) mm = fmaxf(mm, red[t][threadIdx.x]);
+    const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+    if (n < N) scale[e * N + n] = scale_of(mm);
+  } else {  // a block: 32 columns, 4 per warp; lanes walk k in 8-element vectors
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = static_cast<int64_t>(blockIdx.x) * 32 + wid * 4 + j;
+      if (n >= N) break;
+      const __nv_bfloat16* row = we + n * s_n;
+      float m = 0.0f;
+      for (int64_t k8 = lane; k8 < K / 8; k8 += 32) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + k8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h[i]);
+          m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if (lane == 0) scale[e * N + n] = scale_of(m);
+    }
+  }
+}
+
+// 64 (k) x 64 (n) tile: 16-byte loads along the contiguous input dimension into shared memory, then
+// every thread writes 16 consecutive k codes of one n (q[e][n][k], k contiguous) as one 16-byte store.
+template <bool N_FAST>
+__global__ void __launch_bounds__(256) w_quant_vec_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                          int64_t s_e, int64_t s_k, int64_t s_n,
+                                                          const float* __restrict__ scale, uint8_t* __restrict__ q,
+                                                          int64_t ldq) {
+  __shared__ float tile[64][65];  // [k][n]
+  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 64, n0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const __nv_bfloat16* we = w + e * s_e;
+  for (int it = threadIdx.x; it < 512; it += 256) {  // 64 lines x 8 vectors of 8
+    const int line = it >> 3, vec = it & 7;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int64_t kk = N_FAST ? k0 + line : k0 + vec * 8;  // first k of the vector
+    const int64_t nn = N_FAST ? n0 + vec * 8 : n0 + line;   // first n of the vector
+    if (kk < K && nn < N) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(we + kk * s_k + nn * s_n));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 v = __bfloat1622float2(h[j]);
+        f[2 * j] = v.x;
+        f[2 * j + 1] = v.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (N_FAST) tile[line][vec * 8 + j] = f[j];
+      else tile[vec * 8 + j][line] = f[j];
+    }
+  }
+  __syncthreads();
+  const int nl = threadIdx.x >> 2, kq = (threadIdx.x & 3) * 16;  // 64 n x 4 groups of 16 k
+  const int64_t n = n0 + nl, k = k0 + kq;
+  if (n >= N || k >= K) return;
+  const float s = __ldg(scale + e * N + n);
+  uint32_t wds[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint32_t wv = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) wv |= static_cast<uint32_t>(to_e4m3(tile[kq + 4 * g + b][nl] / s)) << (8 * b);
+    wds[g] = wv;
+  }
+  uint8_t* dst = q + (e * N + n) * ldq + k;
+  if (k + 16 <= K) {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+  } else {
+    for (int i = 0; i < K - k; ++i) dst[i] = static_cast<uint8_t>(wds[i >> 2] >> (8 * (i & 3)));
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -240,13 +348,28 @@ extern "C" int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool n_fast = s_n == 1;
   const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(w);
-  const dim3 agrid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>(E));
-  if (n_fast) w_amax_kernel<true><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
-  else w_amax_kernel<false><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
-  if (K > 0) {
-    const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
-    if (n_fast) w_quant_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
-    else w_quant_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+  const int64_t fast_extent = n_fast ? N : K;
+  const int64_t slow_stride = n_fast ? s_k : s_n;
+  const bool vec = aligned16(w) && fast_extent % 8 == 0 && slow_stride % 8 == 0 && s_e % 8 == 0 &&
+                   (n_fast || s_k == 1) && ldq % 16 == 0 && (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
+  if (vec) {
+    const dim3 agrid(static_cast<unsigned>(n_fast ? (N + 255) / 256 : (N + 31) / 32), static_cast<unsigned>(E));
+    if (n_fast) w_amax_vec_kernel<true><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
+    else w_amax_vec_kernel<false><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
+    if (K > 0) {
+      const dim3 grid(static_cast<unsigned>((N + 63) / 64), static_cast<unsigned>((K + 63) / 64), static_cast<unsigned>(E));
+      if (n_fast) w_quant_vec_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+      else w_quant_vec_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+    }
+  } else {
+    const dim3 agrid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>(E));
+    if (n_fast) w_amax_kernel<true><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
+    else w_amax_kernel<false><<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale);
+    if (K > 0) {
+      const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>(E));
+      if (n_fast) w_quant_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+      else w_quant_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
