@@ -127,7 +127,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
     const float* __restrict__ scale, int64_t n_max, const int32_t* __restrict__ n_dev,
     const int64_t* __restrict__ dst_rank, const int64_t* __restrict__ dst_row,
     const unsigned long long* __restrict__ peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
-    int64_t row_vec, int64_t n_src, unsigned int* __restrict__ status, PushSignal sig) {
+    int64_t row_vec, int64_t n_src, unsigned int* __restrict__ status, PushSignal sig,
+    const int64_t* __restrict__ rotate) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -136,7 +137,16 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) push_rows_kernel(
     const int64_t c = __ldg(n_dev);
     n = c < n ? (c > 0 ? c : 0) : n;
   }
-  for (int64_t i = warp0; i < n; i += nwarps) {
+  // rotation: row slot j handles entry (j + *rotate) mod n, so that ranks whose entries are sorted by
+  // destination start on different destinations instead of all writing to rank 0 first
+  int64_t rot = 0;
+  if (rotate != nullptr && n > 0) {
+    rot = __ldg(rotate) % n;
+    if (rot < 0) rot += n;
+  }
+  for (int64_t j = warp0; j < n; j += nwarps) {
+    int64_t i = j + rot;
+    if (i >= n) i -= n;
     const int64_t s = src_idx != nullptr ? __ldg(src_idx + i) : i;
     const int64_t r = __ldg(dst_rank + i);
     const int64_t row = __ldg(dst_row + i);
@@ -249,7 +259,8 @@ extern "C" int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, con
                              const float* scale, int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank,
                              const int64_t* dst_row, const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
                              int64_t row_elems, const unsigned long long* flag_bases,
-                             unsigned long long* counter, unsigned long long seq, int64_t rank, void* stream) {
+                             unsigned long long* counter, unsigned long long seq, int64_t rank,
+                             const int64_t* rotate, void* stream) {
   using namespace mgf;
   if (n_max < 0 || row_elems < 0 || n_src < 0) return MGF_ERR_INVALID_ARGUMENT;
   if (flag_bases != nullptr && (counter == nullptr || rank < 0 || rank >= world)) return MGF_ERR_INVALID_ARGUMENT;
@@ -263,7 +274,7 @@ extern "C" int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, con
   if (status == nullptr) return MGF_ERR_CUDA;
   push_rows_kernel<<<grid_for(n_max), 32 * kWarpsPerBlock, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(src), ld_src, src_idx, scale, n_max, n_dev, dst_rank, dst_row, peer_bases,
-      world, dst_rows, ld_dst, row_elems / 8, n_src, status, sig);
+      world, dst_rows, ld_dst, row_elems / 8, n_src, status, sig, rotate);
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }
 

@@ -662,7 +662,7 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
                     const std::optional<Tensor>& n_dev, const Tensor& dst_rank, const Tensor& dst_row,
                     const Tensor& peer_bases, int64_t dst_rows, int64_t ld_dst, int64_t n_max,
                     const std::optional<Tensor>& flag_bases, const std::optional<Tensor>& counter, int64_t seq,
-                    int64_t rank) {
+                    int64_t rank, const std::optional<Tensor>& rotate) {
   check_rows(src, "src");
   const c10::cuda::CUDAGuard guard(src.device());
   TORCH_CHECK(dst_rank.scalar_type() == at::kLong && dst_row.scalar_type() == at::kLong &&
@@ -687,6 +687,9 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
     TORCH_CHECK(n_dev->scalar_type() == at::kInt && n_dev->numel() >= 1, "push_rows: n_dev must be int32");
     nd = n_dev->data_ptr<int32_t>();
   }
+  if (rotate.has_value())
+    TORCH_CHECK(rotate->is_cuda() && rotate->scalar_type() == at::kLong && rotate->numel() >= 1,
+                "push_rows: rotate must be an int64 device scalar");
   const unsigned long long* fb = nullptr;
   unsigned long long* ctr = nullptr;
   if (flag_bases.has_value()) {
@@ -701,7 +704,9 @@ void push_rows_cuda(const Tensor& src, const std::optional<Tensor>& src_idx, con
                              dst_rank.data_ptr<int64_t>(), dst_row.data_ptr<int64_t>(),
                              reinterpret_cast<const unsigned long long*>(peer_bases.data_ptr<int64_t>()),
                              peer_bases.numel(), dst_rows, ld_dst, src.size(1), fb, ctr,
-                             static_cast<unsigned long long>(seq), rank, at::cuda::getCurrentCUDAStream().stream()),
+                             static_cast<unsigned long long>(seq), rank,
+                             rotate.has_value() ? rotate->data_ptr<int64_t>() : nullptr,
+                             at::cuda::getCurrentCUDAStream().stream()),
                "push_rows");
 }
 
@@ -905,7 +910,7 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def(
       "push_rows(Tensor src, Tensor? src_idx, Tensor? scale, Tensor? n_dev, Tensor dst_rank, Tensor dst_row,"
       " Tensor peer_bases, int dst_rows, int ld_dst, int n_max, Tensor? flag_bases=None, Tensor? counter=None,"
-      " int seq=0, int rank=0) -> ()");
+      " int seq=0, int rank=0, Tensor? rotate=None) -> ()");
   m.def("wait_flags(Tensor flags, int seq, int timeout_ns) -> ()");
   m.def("fp8_quantize_rows(Tensor x) -> (Tensor, Tensor)");
   m.def("fp8_quantize_cols(Tensor x) -> (Tensor, Tensor)");

@@ -301,6 +301,7 @@ class PeerBuffers:
         self.rank = dist.get_rank(group)
         self.local = {k: torch.empty(v, dtype=dtype, device=device) for k, v in shapes.items()}
         self.flags = torch.zeros(self.world, dtype=torch.int64, device=device)
+        self.next_rank = torch.full((1,), (self.rank + 1) % self.world, dtype=torch.int64, device=device)
         self.counters = torch.zeros(4, dtype=torch.int64, device=device)  # one per push kind
         self.seq = 0
         from ._ext import ipc_handle
@@ -345,12 +346,17 @@ class PeerBuffers:
         self.wait(self.push_async(kind, src, src_idx, scale, n_dev, dst_rank, dst_row, target, dst_rows, n_max))
 
     def push_async(self, kind: int, src, src_idx, scale, n_dev, dst_rank, dst_row, target: str, dst_rows: int,
-                   n_max: int) -> int:
-        """The push of push() without the wait, on the current stream; returns its sequence number."""
+                   n_max: int, rotate: torch.Tensor | None = None) -> int:
+        """The push of push() without the wait, on the current stream; returns its sequence number.
+        Entries sorted by destination rank are visited from the first one bound for the next rank
+        (`rotate`, default: counted from dst_rank on the device), so the ranks' pushes start on
+        different destinations instead of all on rank 0."""
         self.seq += 1
+        if rotate is None and n_dev is None:
+            rotate = (dst_rank < self.next_rank).sum().view(1)
         torch.ops.grouped_mm.push_rows(src, src_idx, scale, n_dev, dst_rank, dst_row, self.bases[target], dst_rows,
                                        src.shape[1], n_max, self.bases["flags"], self.counters[kind:kind + 1],
-                                       self.seq, self.rank)
+                                       self.seq, self.rank, rotate)
         return self.seq
 
     def signal(self) -> int:
@@ -499,13 +505,19 @@ def _pipelined_dispatch_up(x, w_up, b_up, st):
         src = st.copy_token[perm]
         d_rank = plan["dst_rank"][perm]
         d_row = plan["dst_row"][perm]
-        seq_a = bufs.push_async(0, x, src, None, n_a, d_rank, d_row, "rows", st.cap, n)
+        # rotations: the first-half entries are ascending in destination rank, the second half (flipped)
+        # descending; start each on the rank after this one
+        nxt = bufs.next_rank
+        rot_a = (first & (plan["dst_rank"] < nxt)).sum().view(1)
+        rot_b = (~first & (plan["dst_rank"] > nxt)).sum().view(1)
+        seq_a = bufs.push_async(0, x, src, None, n_a, d_rank, d_row, "rows", st.cap, n, rotate=rot_a)
         main = torch.cuda.current_stream()
         side = bufs.side_stream
         side.wait_stream(main)
         with torch.cuda.stream(side):
-            seq_b = bufs.push_async(1, x, src.flip(0), None, n_b, d_rank.flip(0), d_row.flip(0), "rows", st.cap, n)
-        for t in (src, d_rank, d_row, n_b):
+            seq_b = bufs.push_async(1, x, src.flip(0), None, n_b, d_rank.flip(0), d_row.flip(0), "rows", st.cap, n,
+                                    rotate=rot_b)
+        for t in (src, d_rank, d_row, n_b, rot_b):
             t.record_stream(side)
         bufs.wait(seq_a)
     rows = bufs.local["rows"]

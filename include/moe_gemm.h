@@ -180,12 +180,14 @@ int mgf_combine_rows(const void* rows, int64_t ld_rows, int64_t n_rows, const in
  * written (release, system scope) into slot `rank` of every rank's flag array (flag_bases: device
  * array of `world` addresses of uint64 [world] flag arrays, IPC-mapped); `counter` is a zeroed
  * device uint64 of this rank that the launch uses and leaves at zero.  Readers then call
- * mgf_wait_flags on their own flag array instead of a collective barrier. */
+ * mgf_wait_flags on their own flag array instead of a collective barrier.
+ * rotate (optional device int64): entries are visited starting at index *rotate (mod n), so that ranks
+ * whose entries are sorted by destination do not all write to the same rank at the same time. */
 int mgf_push_rows(const void* src, int64_t ld_src, int64_t n_src, const int64_t* src_idx, const float* scale,
                   int64_t n_max, const int32_t* n_dev, const int64_t* dst_rank, const int64_t* dst_row,
                   const unsigned long long* peer_bases, int64_t world, int64_t dst_rows, int64_t ld_dst,
                   int64_t row_elems, const unsigned long long* flag_bases, unsigned long long* counter,
-                  unsigned long long seq, int64_t rank, void* stream);
+                  unsigned long long seq, int64_t rank, const int64_t* rotate, void* stream);
 
 /* Wait on `stream` until flags[s] >= seq for every s < world (every rank's push with sequence
  * number seq has landed here), at most timeout_ns; a wait that runs out records
