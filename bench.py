@@ -497,15 +497,20 @@ def ep_parity_check(args, world, rank, device):
                     f"transport {args.transport}" + (" + overlap" if args.ep_overlap else "")}
 
 
-def roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=False):
-    """Live per-kernel roofline of the step: achieved TFLOP/s of the dominant operator (FLOPs per
-    launch / its CUDA-event average) against the measured burst bf16 peak, the sustained one beside."""
+def roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=False, steps=None):
+    """Live per-kernel roofline of the step: achieved TFLOP/s of the dominant operator (its FLOPs per
+    step / its CUDA-event time per step; an operator run as several launches over expert ranges counts
+    all of them) against the measured burst bf16 peak, the sustained one beside."""
     names = [k for k in ops if k in OP_FLOP_UNITS]
     if not names:
         return None
+
+    def per_step_ms(v):
+        return v["total_ms"] / steps if steps else v["avg_ms"]
+
     name = max(names, key=lambda k: ops[k]["total_ms"])
     fl = OP_FLOP_UNITS[name] * float(local_rows) * H * I
-    ach = fl / (ops[name]["avg_ms"] * 1e-3) / 1e12
+    ach = fl / (per_step_ms(ops[name]) * 1e-3) / 1e12
     peak, peak_name = peaks["bf16_tflops"], f"{peak_src} bf16_tflops (burst)"
     if fp8:  # no measured e4m3 peak on this pool: the nominal dense figure
         peak, peak_name = 4500.0, "nominal e4m3 dense 4.5 PFLOP/s (no measured fp8 peak)"
@@ -519,7 +524,8 @@ def roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=False):
             "traffic": tr, "traffic_source": (traffic or {}).get("how") if tr else None,
             "algorithmic_flop_per_launch": fl,
             "ops": {k: {"avg_ms": round(v["avg_ms"], 4), "launches": v["launches"],
-                        "tflops": OP_FLOP_UNITS.get(k, 0) * float(local_rows) * H * I / (v["avg_ms"] * 1e-3) / 1e12}
+                        "ms_per_step": round(per_step_ms(v), 4),
+                        "tflops": OP_FLOP_UNITS.get(k, 0) * float(local_rows) * H * I / (per_step_ms(v) * 1e-3) / 1e12}
                     for k, v in ops.items()}}
 
 
@@ -588,7 +594,7 @@ def extra_workloads(args, mgf, device, peaks, peak_src):
             ms = time_steps(step, steps, 0)
             timer.uninstall()
             fl = (4.0 if fwd else 18.0) * M * H * I
-            roof = roofline_entry(timer.summary(), M, H, I, peaks, peak_src)
+            roof = roofline_entry(timer.summary(), M, H, I, peaks, peak_src, steps=steps)
             out[name] = {"ms_per_step": ms, "tflops": fl / (ms * 1e-3) / 1e12, "routed_rows": M, "steps": steps,
                          "E": E, "H": H, "I": I, "tokens": tokens, "topk": topk,
                          "ops": roof["ops"] if roof else None}
@@ -769,7 +775,7 @@ def main():
     value = flops_all / (ms_max * 1e-3) / 1e12
     per_gpu = value / world
     ours_launches = sum(v["launches"] for k, v in ops.items() if k in OP_FLOP_UNITS or k.startswith("ep_"))
-    roof = roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=args.fp8) if ops else None
+    roof = roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=args.fp8, steps=args.steps) if ops else None
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -798,7 +804,7 @@ def main():
             "gemm_ms_per_step": gemm, "ep_ms_per_step": comm, "other_ms_per_step": ms - gemm - comm,
             "sm_mhz_median": mhz,
             "gemm_ms_at_max_clock": gemm * mhz / 1965.0 if mhz else None,
-            "ep_ops_ms": {k: round(v["avg_ms"], 4) for k, v in ops.items() if k.startswith("ep_")}}
+            "ep_ops_ms_per_step": {k: round(v["total_ms"] / args.steps, 4) for k, v in ops.items() if k.startswith("ep_")}}
 
     # torch._grouped_mm + eager bias/SwiGLU on the same inputs (single GPU only)
     if world == 1 and not args.no_compare and not args.fp8:

@@ -248,7 +248,7 @@ __device__ void build_schedule(const Params& p, const SchedSmem& s, int lane) {
       if constexpr (!RAGGED_K) {
         cnt = e < p.group_begin ? 0 : (int)((ep - sp + TM - 1) / TM) * p.n_tiles;
       } else {
-        cnt = p.m_tiles * p.n_tiles;
+        cnt = e < p.group_begin ? 0 : p.m_tiles * p.n_tiles;
       }
     }
     int inc = cnt;
@@ -1280,8 +1280,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
   p.aux_v8 = v8_ok(g.aux, g.ld_aux) ? 1 : 0;
   p.d_v8 = v8_ok(g.d, g.ldd) ? 1 : 0;
   p.d_rows = reinterpret_cast<const long long*>(g.d_row_ptrs);
-  if (g.group_begin < 0 || g.group_begin > g.num_groups || (ragged_k && g.group_begin != 0))
-    return MGF_ERR_INVALID_ARGUMENT;
+  if (g.group_begin < 0 || g.group_begin > g.num_groups) return MGF_ERR_INVALID_ARGUMENT;
   p.group_begin = g.group_begin;
   if (scatter) p.d_v8 = (g.n % 16) == 0 ? 1 : 0;  // per-row address alignment is checked in the kernel
   p.d2_v8 = v8_ok(g.d2, g.ldd2) ? 1 : 0;

@@ -128,14 +128,15 @@ void launch_ragged_m(int epi, const Tensor& a, const Tensor& b, const Tensor& of
 // Ragged-K launch: mat_a [M, total_K] is the transposed view (stride(0) == 1) of a row-major
 // [total_K, M] matrix, mat_b [total_K, N] is row-major; returns (D [E, M, N], db [E, N] or undefined).
 std::tuple<Tensor, Tensor> ragged_k_launch(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs,
-                                           bool bias_grad, const char* what) {
+                                           bool bias_grad, const char* what, const Tensor* out_in = nullptr,
+                                           const Tensor* db_in = nullptr, int64_t group_begin = 0) {
   TORCH_CHECK(mat_a.stride(0) == 1, what,
               ": ragged-K needs mat_a as a transposed row-major matrix (stride(0) == 1)");
   TORCH_CHECK(mat_b.stride(1) == 1, what, ": ragged-K needs a row-major mat_b");
   TORCH_CHECK(mat_a.size(1) == mat_b.size(0), "contraction dimension of mat_a and mat_b must match");
   const int64_t E = offs.size(0), M = mat_a.size(0), N = mat_b.size(1);
-  Tensor out = at::empty_strided({E, M, N}, {M * padded(N), padded(N), 1}, mat_a.options());
-  Tensor db;
+  Tensor out = out_in != nullptr ? *out_in : at::empty_strided({E, M, N}, {M * padded(N), padded(N), 1}, mat_a.options());
+  Tensor db = db_in != nullptr ? *db_in : Tensor();
   mgf_gemm_desc g = base_desc();
   g.epilogue = MGF_EPI_WGRAD;
   g.num_groups = static_cast<int32_t>(E);
@@ -154,13 +155,36 @@ std::tuple<Tensor, Tensor> ragged_k_launch(const Tensor& mat_a, const Tensor& ma
   Tensor workspace = at::zeros({1}, mat_a.options().dtype(at::kInt));
   g.workspace = workspace.data_ptr<int32_t>();
   if (bias_grad) {
-    db = at::empty({E, N}, mat_a.options());
+    if (!db.defined()) db = at::empty({E, N}, mat_a.options());
     g.d2 = db.data_ptr();
     g.ldd2 = db.stride(0);
   }
+  g.group_begin = static_cast<int32_t>(group_begin);
   g.sm_carveout = sm_carveout_for(mat_a);
   check_launch(mgf_grouped_gemm_launch(&g, at::cuda::getCurrentCUDAStream().stream()), what);
   return {out, db};
+}
+
+// In-place forms over a range of groups, for launches split by expert range (group_begin): the weight
+// + bias gradient into dW [E, m, n] (unit column stride, rows padded to 16 bytes) and db [E, n], and the
+// down-proj dgrad + SwiGLU backward into grad_aux [M, 2I].
+void wgrad_bias_into_cuda(const Tensor& mat_a, const Tensor& mat_b, const Tensor& offs, const Tensor& dw,
+                          const Tensor& db, int64_t group_begin) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda() && mat_a.scalar_type() == at::kBFloat16 &&
+                  mat_b.scalar_type() == at::kBFloat16 && dw.scalar_type() == at::kBFloat16 &&
+                  db.scalar_type() == at::kBFloat16,
+              "grouped_mm_wgrad_bias: bf16 CUDA tensors");
+  check_offs(offs, mat_a);
+  const int64_t E = offs.size(0);
+  TORCH_CHECK(dw.dim() == 3 && dw.size(0) == E && dw.size(1) == mat_a.size(0) && dw.size(2) == mat_b.size(1) &&
+                  dw.stride(2) == 1 && dw.stride(1) % 8 == 0 && dw.stride(0) % 8 == 0,
+              "grouped_mm_wgrad_bias: dw must be [E, m, n] with unit column stride and 16-byte row pitch");
+  TORCH_CHECK(db.dim() == 2 && db.size(0) == E && db.size(1) == mat_b.size(1) && db.stride(1) == 1 &&
+                  db.stride(0) % 8 == 0,
+              "grouped_mm_wgrad_bias: db must be [E, n] row-major");
+  TORCH_CHECK(group_begin >= 0 && group_begin <= E, "grouped_mm_wgrad_bias: group_begin out of range");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  ragged_k_launch(mat_a, mat_b, offs, true, "grouped_mm_wgrad_bias", &dw, &db, group_begin);
 }
 
 // Layout normalisation for the general `grouped_mm::mm` layouts the kernels do not read directly
@@ -380,6 +404,28 @@ void swiglu_bwd_into_cuda(const Tensor& grad_output, const Tensor& down_w_t, con
   const Tensor grad = grad_packed.view(at::kBFloat16);
   launch_ragged_m(MGF_EPI_SWIGLU_BWD, grad_output.contiguous(), down_w_t, offs, nullptr, grad, nullptr, &aux, alpha,
                   limit, false, "grouped_mm_swiglu_bwd");
+}
+
+void swiglu_bwd_range_into_cuda(const Tensor& grad_output, const Tensor& down_w_t, const Tensor& offs,
+                                const Tensor& aux, const Tensor& grad_aux, double alpha, double limit,
+                                int64_t group_begin) {
+  TORCH_CHECK(grad_output.is_cuda() && grad_output.dim() == 2 && grad_output.stride(1) == 1 &&
+                  grad_output.scalar_type() == at::kBFloat16 && down_w_t.dim() == 3 &&
+                  down_w_t.scalar_type() == at::kBFloat16,
+              "grouped_mm_swiglu_bwd: bf16 grad_output [M, H] row-major and down_w_t [E, H, I]");
+  check_offs(offs, grad_output);
+  TORCH_CHECK(down_w_t.size(0) == offs.size(0) && grad_output.size(1) == down_w_t.size(1),
+              "grouped_mm_swiglu_bwd: shapes");
+  TORCH_CHECK(aux.scalar_type() == at::kBFloat16 && grad_aux.scalar_type() == at::kBFloat16 && aux.dim() == 2 &&
+                  grad_aux.dim() == 2 && aux.size(0) == grad_output.size(0) && grad_aux.size(0) == aux.size(0) &&
+                  aux.size(1) == 2 * down_w_t.size(2) && grad_aux.size(1) == aux.size(1) && aux.stride(1) == 1 &&
+                  grad_aux.stride(1) == 1,
+              "grouped_mm_swiglu_bwd: aux and grad_aux must be row-major bf16 [M, 2*I]");
+  TORCH_CHECK(group_begin >= 0 && group_begin <= offs.size(0), "grouped_mm_swiglu_bwd: group_begin out of range");
+  const c10::cuda::CUDAGuard guard(grad_output.device());
+  if (grad_output.size(0) == 0) return;
+  launch_ragged_m(MGF_EPI_SWIGLU_BWD, grad_output, down_w_t, offs, nullptr, grad_aux, nullptr, &aux, alpha, limit,
+                  false, "grouped_mm_swiglu_bwd", false, group_begin);
 }
 
 // ---------------------------------------------------------------- grouped_mm::mm_swiglu_noaux
@@ -893,6 +939,10 @@ TORCH_LIBRARY(grouped_mm, m) {
       "swiglu_range_into(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor bias, Tensor(a!)? aux_out,"
       " Tensor(b!) swiglu_out, float swiglu_alpha, float swiglu_limit, bool store_aux, int group_begin) -> ()");
   m.def(
+      "swiglu_bwd_range_into(Tensor grad_output, Tensor down_w_t, Tensor offs, Tensor aux_biased_acc,"
+      " Tensor(a!) grad_aux, float swiglu_alpha, float swiglu_limit, int group_begin) -> ()");
+  m.def("wgrad_bias_into(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor(a!) dw, Tensor(b!) db, int group_begin) -> ()");
+  m.def(
       "swiglu_bwd_into(Tensor grad_output, Tensor down_w_t, Tensor offs, Tensor aux_packed,"
       " Tensor(a!) grad_gate_up_packed, float swiglu_alpha, float swiglu_limit) -> ()");
   m.def("mm_fp8(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor scale_a, Tensor scale_b, Tensor? bias) -> Tensor");
@@ -929,6 +979,8 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("mm_swiglu_noaux", &mm_swiglu_noaux_cuda);
   m.impl("swiglu_into", &swiglu_into_cuda);
   m.impl("swiglu_range_into", &swiglu_range_into_cuda);
+  m.impl("swiglu_bwd_range_into", &swiglu_bwd_range_into_cuda);
+  m.impl("wgrad_bias_into", &wgrad_bias_into_cuda);
   m.impl("swiglu_bwd_into", &swiglu_bwd_into_cuda);
   m.impl("mm_swiglu_bwd", &mm_swiglu_bwd_cuda);
   m.impl("mm_wgrad_bias", &mm_wgrad_bias_cuda);

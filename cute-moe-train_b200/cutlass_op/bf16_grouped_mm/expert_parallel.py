@@ -486,6 +486,27 @@ class _PeerCombine(torch.autograd.Function):
         return st.bufs.local["grows"].view(st.cap, g.shape[1]), grad_w, None
 
 
+def _split_halves(st) -> dict:
+    """The routed copies split by their owner's local-expert half (first e_local/2 experts, then the
+    rest), as index arrays for the two-part pushes: first-half entries ascending in destination rank,
+    second half flipped (descending); counts and start rotations as device scalars (no host sync)."""
+    if getattr(st, "halves", None) is not None:
+        return st.halves
+    plan = st.plan
+    el = plan["offs"].numel()
+    h = el // 2
+    first = torch.remainder(st.e_sorted, el) < h
+    perm = torch.argsort((~first).to(torch.int8), stable=True)  # first-half copies, then the rest
+    n_a = first.sum(dtype=torch.int32).view(1)
+    nxt = st.bufs.next_rank
+    st.halves = {
+        "h": h, "perm": perm, "n_a": n_a, "n_b": (st.n - n_a).to(torch.int32),
+        "src": st.copy_token[perm], "d_rank": plan["dst_rank"][perm], "d_row": plan["dst_row"][perm],
+        "rot_a": (first & (plan["dst_rank"] < nxt)).sum().view(1),
+        "rot_b": (~first & (plan["dst_rank"] > nxt)).sum().view(1)}
+    return st.halves
+
+
 def _pipelined_dispatch_up(x, w_up, b_up, st):
     """Dispatch + up-projection in two halves of the local experts, so the second half's rows cross
     NVLink while the first half's GEMM runs: push the copies bound for every owner's first e_local/2
@@ -498,18 +519,9 @@ def _pipelined_dispatch_up(x, w_up, b_up, st):
     h = el // 2
     n = st.n
     with timed("ep_peer_dispatch"):
-        first = torch.remainder(st.e_sorted, el) < h
-        perm = torch.argsort((~first).to(torch.int8), stable=True)  # first-half copies, then the rest
-        n_a = first.sum(dtype=torch.int32).view(1)
-        n_b = (n - n_a).to(torch.int32)
-        src = st.copy_token[perm]
-        d_rank = plan["dst_rank"][perm]
-        d_row = plan["dst_row"][perm]
-        # rotations: the first-half entries are ascending in destination rank, the second half (flipped)
-        # descending; start each on the rank after this one
-        nxt = bufs.next_rank
-        rot_a = (first & (plan["dst_rank"] < nxt)).sum().view(1)
-        rot_b = (~first & (plan["dst_rank"] > nxt)).sum().view(1)
+        sp = _split_halves(st)
+        src, d_rank, d_row, n_a, n_b, rot_a, rot_b = (sp[k] for k in ("src", "d_rank", "d_row", "n_a", "n_b",
+                                                                       "rot_a", "rot_b"))
         seq_a = bufs.push_async(0, x, src, None, n_a, d_rank, d_row, "rows", st.cap, n, rotate=rot_a)
         main = torch.cuda.current_stream()
         side = bufs.side_stream
@@ -531,6 +543,52 @@ def _pipelined_dispatch_up(x, w_up, b_up, st):
         torch.ops.grouped_mm.swiglu_range_into(rows, w_up, offs, b_up, aux, s, st.alpha, st.limit, True, h)
     main.wait_stream(side)
     return s, aux
+
+
+def _pipelined_combine_bwd_down(g, scale, s, w_down, aux, st):
+    """Backward counterpart of _pipelined_dispatch_up: push the output gradient rows bound for every
+    owner's first expert half (main stream) and the rest (side stream), run the down-proj weight + bias
+    gradient and the dgrad + SwiGLU backward over experts [0, h) while the second half lands, then
+    over [h, e_local) (group_begin) into the same outputs."""
+    bufs, plan = st.bufs, st.plan
+    offs = plan["offs"]
+    sp = _split_halves(st)
+    h = sp["h"]
+    perm = sp["perm"]
+    sc = scale[perm] if scale is not None else None
+    main = torch.cuda.current_stream()
+    side = bufs.side_stream
+    with timed("ep_peer_combine_bwd"):
+        seq_a = bufs.push_async(2, g, sp["src"], sc, sp["n_a"], sp["d_rank"], sp["d_row"], "grows", st.cap, st.n,
+                                rotate=sp["rot_a"])
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            sc_b = sc.flip(0) if sc is not None else None
+            src_b, dr_b, drow_b = sp["src"].flip(0), sp["d_rank"].flip(0), sp["d_row"].flip(0)
+            seq_b = bufs.push_async(3, g, src_b, sc_b, sp["n_b"], dr_b, drow_b, "grows", st.cap, st.n,
+                                    rotate=sp["rot_b"])
+        g.record_stream(side)
+        bufs.wait(seq_a)
+    grows = bufs.local["grows"]
+    el, i_dim, h_dim = w_down.shape
+    dev, dt = grows.device, grows.dtype
+    g_wd = torch.empty_strided((el, i_dim, h_dim), (i_dim * _padded_cols(h_dim), _padded_cols(h_dim), 1), dtype=dt,
+                               device=dev)
+    g_bd = torch.empty((el, h_dim), dtype=dt, device=dev)
+    grad_aux = torch.empty_strided(aux.shape, (_padded_cols(aux.shape[1]), 1), dtype=dt, device=dev)
+    s_t = s.transpose(-2, -1)
+    w_t = w_down.transpose(-2, -1)
+    with timed("down_wgrad_bias"):
+        torch.ops.grouped_mm.wgrad_bias_into(s_t, grows, offs[:h], g_wd[:h], g_bd[:h], 0)
+    with timed("down_dgrad_swiglu_bwd"):
+        torch.ops.grouped_mm.swiglu_bwd_range_into(grows, w_t[:h], offs[:h], aux, grad_aux, st.alpha, st.limit, 0)
+    bufs.wait(seq_b)
+    with timed("down_wgrad_bias"):
+        torch.ops.grouped_mm.wgrad_bias_into(s_t, grows, offs, g_wd, g_bd, h)
+    with timed("down_dgrad_swiglu_bwd"):
+        torch.ops.grouped_mm.swiglu_bwd_range_into(grows, w_t, offs, aux, grad_aux, st.alpha, st.limit, h)
+    main.wait_stream(side)
+    return g_wd, g_bd, grad_aux
 
 
 def _padded_cols(n: int) -> int:
@@ -583,14 +641,17 @@ class _PeerMoE(torch.autograd.Function):
         offs = plan["offs"]
         g = g.contiguous()
         scale = w_flat[st.order].contiguous() if w_flat is not None else None
-        with timed("ep_peer_combine_bwd"):
-            bufs.push(2, g, st.copy_token, scale, None, plan["dst_rank"], plan["dst_row"], "grows", st.cap, st.n)
         grows = bufs.local["grows"]
-        with timed("down_wgrad_bias"):
-            g_wd, g_bd = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), grows, offs)
-        with timed("down_dgrad_swiglu_bwd"):
-            grad_aux = torch.ops.grouped_mm.mm_swiglu_bwd(grows, w_down.transpose(-2, -1), offs, aux, st.alpha,
-                                                          st.limit)
+        if st.pipeline and offs.numel() >= 2:
+            g_wd, g_bd, grad_aux = _pipelined_combine_bwd_down(g, scale, s, w_down, aux, st)
+        else:
+            with timed("ep_peer_combine_bwd"):
+                bufs.push(2, g, st.copy_token, scale, None, plan["dst_rank"], plan["dst_row"], "grows", st.cap, st.n)
+            with timed("down_wgrad_bias"):
+                g_wd, g_bd = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), grows, offs)
+            with timed("down_dgrad_swiglu_bwd"):
+                grad_aux = torch.ops.grouped_mm.mm_swiglu_bwd(grows, w_down.transpose(-2, -1), offs, aux, st.alpha,
+                                                              st.limit)
         with timed("up_dgrad"):
             torch.ops.grouped_mm.mm_scatter(grad_aux, w_up.transpose(-2, -1), offs, None, plan["ptr_gret"])
         seq = bufs.signal()

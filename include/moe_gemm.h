@@ -129,8 +129,8 @@ typedef struct mgf_gemm_desc {
                             instead of d + r * ldd (d and ldd are then unused).  The expert-parallel
                             combine writes each expert output straight into its source rank's buffer
                             this way, fusing the transfer into the GEMM epilogue. */
-  int32_t group_begin;   /* ragged-M only: groups 0 .. group_begin-1 are skipped (no tile computed, no
-                            row written); 0 = all.  Lets a caller run a grouped GEMM in two launches
+  int32_t group_begin;   /* groups 0 .. group_begin-1 are skipped (no tile computed, nothing written --
+                            for WGRAD not even the zeros of empty groups); 0 = all.  Lets a caller run a grouped GEMM in two launches
                             over the expert ranges [0, g) and [g, E) of one offs array, e.g. while the
                             rows of the second range are still arriving. */
 } mgf_gemm_desc;
