@@ -270,3 +270,29 @@ def test_group_range_launches_equal_one_launch():
             assert torch.equal(s, s_ref) and torch.equal(aux, aux_ref), cg
         finally:
             del os.environ["MGF_CTA_GROUP"]
+
+
+def test_backward_range_launches_equal_one_launch():
+    """The weight + bias gradient (ragged-K) and the dgrad + SwiGLU backward split into the expert
+    ranges [0, h) and [h, E) (group_begin) equal the single launches bit for bit, empty groups included."""
+    _lib()
+    from cutlass_op.bf16_grouped_mm.workloads import small_case
+
+    x, w_up, b_up, w_down, b_down, offs, gout = small_case(6, 256, 128, [300, 0, 517, 41, 600, 1], seed=43)
+    x, w_up, b_up, w_down, offs, gout = (t.cuda() for t in (x, w_up, b_up, w_down, offs, gout))
+    s, aux = torch.ops.grouped_mm.mm_swiglu(x, w_up, offs, b_up, 1.702, 7.0)
+    h = 3
+    dw_ref, db_ref = torch.ops.grouped_mm.mm_wgrad_bias(s.transpose(-2, -1), gout, offs)
+    E, I, H = w_down.shape
+    dw = torch.full((E, I, H), float("nan"), dtype=torch.bfloat16, device="cuda")
+    db = torch.full((E, H), float("nan"), dtype=torch.bfloat16, device="cuda")
+    torch.ops.grouped_mm.wgrad_bias_into(s.transpose(-2, -1), gout, offs[:h], dw[:h], db[:h], 0)
+    torch.ops.grouped_mm.wgrad_bias_into(s.transpose(-2, -1), gout, offs, dw, db, h)
+    ga_ref = torch.ops.grouped_mm.mm_swiglu_bwd(gout, w_down.transpose(-2, -1), offs, aux, 1.702, 7.0)
+    ga = torch.full_like(aux, float("nan"))
+    w_t = w_down.transpose(-2, -1)
+    torch.ops.grouped_mm.swiglu_bwd_range_into(gout, w_t[:h], offs[:h], aux, ga, 1.702, 7.0, 0)
+    torch.ops.grouped_mm.swiglu_bwd_range_into(gout, w_t, offs, aux, ga, 1.702, 7.0, h)
+    torch.cuda.synchronize()
+    assert torch.equal(dw, dw_ref) and torch.equal(db, db_ref.to(db.dtype))
+    assert torch.equal(ga, ga_ref)
