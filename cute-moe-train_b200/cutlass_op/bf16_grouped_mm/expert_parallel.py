@@ -719,7 +719,7 @@ def ep_moe_ffn_peer(x: torch.Tensor, expert_idx: torch.Tensor, num_experts: int,
     st.overlap = overlap
     if fused is not None:
         st.alpha, st.limit = fused["alpha"], fused["limit"]
-        st.pipeline = fused.get("pipeline", True)
+        st.pipeline = fused.get("pipeline", False)
         w_flat = router_weights.reshape(-1).float().contiguous() if router_weights is not None else None
         out = _PeerMoE.apply(x, fused["w_up"], fused["b_up"], fused["w_down"], fused["b_down"], w_flat, st)
         bufs.pending_backward = out.requires_grad
@@ -743,7 +743,7 @@ class EPMoEFFN(torch.nn.Module):
     def __init__(self, num_experts: int, hidden: int, inter: int, group=None, device=None, seed: int = 0,
                  swiglu_alpha: float = 1.702, swiglu_limit: float = 7.0, transport: str = "peer",
                  overlap: bool = False, capacity_factor: float = 2.0, fused: bool = True,
-                 pipeline: bool = True):
+                 pipeline: bool = False):
         """transport: "peer" (NVLink pushes, CUDA, world > 1) or "nccl" (all-to-all).  overlap (peer
         transport): push the dispatch's gradient on a side stream under the up-projection weight
         gradient instead of after it.  capacity_factor (peer transport): receive buffers hold
@@ -752,7 +752,9 @@ class EPMoEFFN(torch.nn.Module):
         the down-proj forward / up-proj dgrad epilogues straight into the source ranks (_PeerMoE);
         False: separate push kernels around the FFN (then `overlap` applies).  pipeline (fused peer
         transport, at least 2 local experts): the dispatch and the up-projection run in two halves
-        of the local experts, the second half's push overlapping the first half's GEMM."""
+        of the local experts, the second half's push overlapping the first half's GEMM (and the
+        combine-gradient push likewise with the down-proj backward); off by default since the
+        second tail wave of each split GEMM costs about what the overlap saves."""
         super().__init__()
         self.fused = fused
         self.pipeline = pipeline

@@ -162,9 +162,10 @@ def _transport_worker(rank, world, port, q):
             g0 = torch.randn(T, H, generator=gen).to(torch.bfloat16)
             idx = route_tokens(T, E, K, "zipf", seed=20 + rank)
             res["inputs"] = [x0.float().numpy(), idx.numpy(), w0.numpy(), g0.float().numpy()]
-            for transport in ("nccl", "peer", "peer_unfused", "peer_overlap"):
+            for transport in ("nccl", "peer", "peer_pipeline", "peer_unfused", "peer_overlap"):
                 ffn = EPMoEFFN(E, H, I, device=dev, seed=5, transport=transport.split("_")[0],
-                               overlap=transport.endswith("overlap"), fused=transport == "peer")
+                               overlap=transport.endswith("overlap"), fused=transport in ("peer", "peer_pipeline"),
+                               pipeline=transport == "peer_pipeline")
                 x = x0.to(dev).requires_grad_(True)
                 w = w0.to(dev).requires_grad_(True)
                 for step in range(2):  # the second step reuses the peer buffers
@@ -230,12 +231,14 @@ def test_ep_world2_every_transport_matches_oracle():
     want = ep_reference([torch.from_numpy(i[0]).to(bf) for i in ins], [torch.from_numpy(i[1]) for i in ins],
                         [torch.from_numpy(i[2]) for i in ins], [torch.from_numpy(i[3]).to(bf) for i in ins], *wts)
     for rank in range(2):
-        for transport in ("nccl", "peer", "peer_unfused", "peer_overlap"):
+        for transport in ("nccl", "peer", "peer_pipeline", "peer_unfused", "peer_overlap"):
             _check_ep(transport, [torch.from_numpy(a) for a in res[rank][transport]], want, rank, E // 2)
         for a, b in zip(res[rank]["peer_overlap"], res[rank]["peer_unfused"]):
             assert (a == b).all(), f"rank{rank}: overlap changed the result"
         for a, b in zip(res[rank]["peer"], res[rank]["peer_unfused"]):
             assert (a == b).all(), f"rank{rank}: the fused epilogues changed the result"
+        for a, b in zip(res[rank]["peer_pipeline"], res[rank]["peer"]):
+            assert (a == b).all(), f"rank{rank}: the pipelined halves changed the result"
 
 
 def _overflow_worker(rank, world, port, q):
