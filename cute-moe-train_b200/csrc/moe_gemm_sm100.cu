@@ -53,7 +53,11 @@ constexpr int kRing = 4;                      // tile ids in flight between the 
 constexpr uint64_t kWaitLimitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s per pipeline wait
 constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
 
-template <int BN, int CG, bool B_MN>
+// OB: 2 KB output staging slices per epilogue warp (ragged-K TMA-store epilogue).  OB = 1: one
+// 32 x 32 store per chunk.  OB = 4 (short groups): a warp stages all its chunks of a tile (32 rows x
+// up to 128 columns) and stores them with one TMA store, 4x fewer store operations per tile, at the
+// price of a pipeline stage that tiles of a few K stages do not need.
+template <int BN, int CG, bool B_MN, int OB = 1>
 struct TileCfg {
   static constexpr int A_BYTES = BM * BK * 2;                        // this CTA's 128 rows of A
   static constexpr int BNC = BN / CG;                                // this CTA's columns of B
@@ -64,7 +68,7 @@ struct TileCfg {
   static constexpr int BAR_BYTES = 512;
   static constexpr int SCHED_BYTES = 3 * 4 * (kMaxGroups + 1);
   static constexpr int OUT_CHUNK_BYTES = BM * 32 * 2;                // one 128 x 32 bf16 output chunk
-  static constexpr int OUT_BYTES = kEpiGroups * OUT_CHUNK_BYTES;     // TMA-store staging (ragged-K)
+  static constexpr int OUT_BYTES = kEpiGroups * OUT_CHUNK_BYTES * OB;  // TMA-store staging (ragged-K)
   static constexpr int OUT_OFFSET = (BAR_BYTES + SCHED_BYTES + 1023) / 1024 * 1024;  // after the stages
   static constexpr int BUDGET = 227 * 1024 - 1024 - OUT_OFFSET - OUT_BYTES;
   static constexpr int STAGES = (BUDGET / STAGE_BYTES) > 8 ? 8 : (BUDGET / STAGE_BYTES);
@@ -106,6 +110,7 @@ struct Params {
   int* tile_counter;  // zero-filled device counter: dynamic tile order; nullptr = static striding
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
   int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
+  int small_k;              // ragged-K bf16, single CTAs: one wide TMA store per warp and tile, one stage fewer
 };
 
 struct TileInfo {
@@ -351,11 +356,13 @@ __device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k
 // Stages whose odd-CTA half must be patched first (ragged-K tails, the ones row) are "relayed":
 // the odd CTA counts their bytes on its own barrier, patches, then arrives on the even CTA's
 // patch_done barrier; every other stage counts both CTAs' bytes directly on the even CTA's barrier.
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const Params p) {
-  using Cfg = TileCfg<BN, CG, B_MN>;
+  using Cfg = TileCfg<BN, CG, B_MN, OB>;
+  static_assert(OB == 1 || (EPI == MGF_EPI_WGRAD && OB == 4 && CG == 1 && !F8 && BN != 192),
+                "wide output staging: bf16 single-CTA weight gradient, 64-column-aligned warp halves");
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
   constexpr int KR = (RAGGED_K && F8) ? 128 : BK;  // ragged-K: token rows per stage
   constexpr int KMMA = F8 ? 32 : 16;                // K rows (elements) of one MMA instruction
@@ -880,9 +887,63 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool row_bias = (r == ones_r);
         const bool warp_rows = m0 + q * 32 < p.m;  // this warp holds rows of dW
         const bool warp_active = warp_rows || (ones_r >= q * 32 && ones_r < q * 32 + 32);
-        uint8_t* slice = out_stage + (warp - 2) * (32 * 64);
-        const uint32_t slice_u32 = ptx::smem_u32(slice);
-        if (warp_active) {
+        uint8_t* const slices = out_stage + (warp - 2) * OB * (32 * 64);
+        if (OB == 4 && warp_active) {
+          // wide form: the TMEM loads of two chunks are issued before one wait; the chunks go into
+          // one slab {64 columns, 32 rows, 64-column chunks} (128-byte swizzle: chunk j is 64-column
+          // chunk j / 2, 16-byte units 4 * (j % 2) + g, each at unit ^ (row & 7) within its row's
+          // 128 bytes) and out with one TMA store
+          if (warp_rows) {
+            if (lane == 0) ptx::bulk_wait_read_all();  // the previous tile's store has read the slab
+            __syncwarp();
+          }
+#pragma unroll
+          for (int jb = 0; jb < kChunks; jb += 2) {
+            if (n0 + (c_begin + jb) * 32 >= p.n) break;
+            uint32_t v[2][32];
+            if (ti.nk > 0) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+                if (jb + u < kChunks && n0 + (c_begin + jb + u) * 32 < p.n)
+                  ptx::tmem_ld_32x32b_x32(tbase + (c_begin + jb + u) * 32, v[u]);
+              ptx::tmem_ld_wait();
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int j = jb + u;
+              const int col0 = n0 + (c_begin + j) * 32;
+              if (j >= kChunks || col0 >= p.n) break;
+              uint32_t packed[16];
+#pragma unroll
+              for (int h = 0; h < 16; ++h)
+                packed[h] = ti.nk > 0 ? pack_bf16x2(__uint_as_float(v[u][2 * h]), __uint_as_float(v[u][2 * h + 1])) : 0u;
+              if (warp_rows) {
+                uint8_t* row_base = slices + (j >> 1) * 4096 + lane * 128;
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                  *reinterpret_cast<uint4*>(row_base + (((4 * (j & 1) + g) ^ (lane & 7)) << 4)) =
+                      make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+              }
+              if (row_bias) {
+                uint4* dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                  if (col0 + 8 * g < p.n)
+                    dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+              }
+            }
+          }
+          // one store of the warp's chunks (clipped at m, and at the last 64-column chunk of n)
+          const int col_first = n0 + c_begin * 32;
+          if (warp_rows && col_first < p.n) {
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_4d(&tmD, ptx::smem_u32(slices), 0, m0 + q * 32, col_first / 64, ti.e);
+              ptx::bulk_commit();
+            }
+          }
+        } else if (warp_active) {
 #pragma unroll 1
           for (int c = c_begin; c < c_begin + kChunks; ++c) {
             const int col0 = n0 + c * 32;
@@ -913,12 +974,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int h = 0; h < 16; ++h) packed[h] = 0u;
             }
             if (warp_rows) {
+              const uint32_t slice_u32 = ptx::smem_u32(slices);
               if (lane == 0) ptx::bulk_wait_read_all();  // the slice's previous store has read it
               __syncwarp();
               // 64-byte swizzle (matches the tensor map): 16-byte unit g of row `lane` at g ^ ((lane >> 1) & 3)
 #pragma unroll
               for (int g = 0; g < 4; ++g)
-                *reinterpret_cast<uint4*>(slice + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
+                *reinterpret_cast<uint4*>(slices + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
                     make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
               ptx::fence_proxy_async_smem();
               __syncwarp();
@@ -986,10 +1048,11 @@ static bool encode_bf16(CUtensorMap* m, const void* base, int rank, const uint64
                         CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = get_encode_fn();
   if (fn == nullptr) return false;
-  cuuint64_t d[3];
-  cuuint64_t s[2];
-  cuuint32_t b[3];
-  cuuint32_t e[3] = {1, 1, 1};
+  if (rank < 1 || rank > 4) return false;
+  cuuint64_t d[4];
+  cuuint64_t s[3];
+  cuuint32_t b[4];
+  cuuint32_t e[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     d[i] = dims[i];
     b[i] = box[i];
@@ -1035,12 +1098,12 @@ static bool debug_sync() {
   return v == 1;
 }
 
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1>
 static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD, const Params& p,
                        int grid_in, cudaStream_t st) {
   int grid = grid_in;
-  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG, F8>;
-  constexpr int smem = TileCfg<BN, CG, B_MN>::SMEM_BYTES;
+  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG, F8, OB>;
+  constexpr int smem = TileCfg<BN, CG, B_MN, OB>::SMEM_BYTES;
   static std::mutex mu;
   static bool attr_done[64] = {};
   static int max_clusters[64] = {};
@@ -1131,6 +1194,8 @@ static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, cons
       return b_mn ? launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, true, CG>(tA, tB, tD, p, grid, st)
                   : launch_inst<BN, MGF_EPI_SWIGLU_BWD, false, false, CG>(tA, tB, tD, p, grid, st);
     case MGF_EPI_WGRAD:
+      if constexpr (CG == 1 && BN != 192)
+        if (p.small_k) return launch_inst<BN, MGF_EPI_WGRAD, true, true, 1, false, 4>(tA, tB, tD, p, grid, st);
       return launch_inst<BN, MGF_EPI_WGRAD, true, true, CG>(tA, tB, tD, p, grid, st);
     default:
       return MGF_ERR_INVALID_ARGUMENT;
@@ -1140,6 +1205,8 @@ static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, cons
 // CTA pair (cta_group::2, 256-row tiles) or single CTA (128-row tiles).  Pairs halve the B bytes
 // each SM streams per FLOP; their 256-row tiles waste more rows at group ends, so small groups stay
 // on single CTAs.  MGF_CTA_GROUP=1|2 forces a choice (the tests exercise both).
+constexpr int64_t kSmallKTokens = 256;  // average tokens per group at or below which small_k applies
+
 static int pick_cta_group(bool ragged_k, int64_t total_rows, int num_groups, int64_t m) {
   const char* env = getenv("MGF_CTA_GROUP");
   if (env != nullptr && (env[0] == '1' || env[0] == '2')) return env[0] - '0';
@@ -1422,11 +1489,28 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
       if (!encode_bf16(&tA, g.d, 2, dz, sz, box) || !encode_bf16(&tB, g.d, 2, dz, sz, box)) return MGF_ERR_CUDA;
     }
     tiles_upper = static_cast<int64_t>(p.m_tiles) * n_tiles * g.num_groups;
-    // dW [E, m, n] for the epilogue's TMA tile stores: 32 x 32 boxes, 64-byte swizzle
-    const uint64_t dD[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.num_groups)};
+    // Short groups (a few K stages per tile): the tile time is its dW store epilogue, so each warp
+    // stores its 32 rows x BN/2 columns with one TMA store (the wide form; n a multiple of 64 so
+    // that 64-column chunks never cross a row end).  MGF_WGRAD_SMALL_K=0|1 forces the choice.
+    if (!f8 && cg == 1 && bn != 192 && (g.n % 64) == 0) {
+      const char* env = getenv("MGF_WGRAD_SMALL_K");
+      if (env != nullptr && (env[0] == '0' || env[0] == '1')) p.small_k = env[0] - '0';
+      else p.small_k = (g.total_rows / g.num_groups <= kSmallKTokens) ? 1 : 0;
+    }
     const uint64_t sD[2] = {static_cast<uint64_t>(g.ldd) * 2, static_cast<uint64_t>(g.ldd_batch) * 2};
-    const uint32_t bD[3] = {32, 32, 1};
-    if (!encode_bf16(&tD, g.d, 3, dD, sD, bD, CU_TENSOR_MAP_SWIZZLE_64B)) return MGF_ERR_CUDA;
+    if (p.small_k) {
+      // dW as {64 columns, m rows, n / 64 chunks, E}: boxes {64, 32, BN / 128, 1}, 128-byte swizzle
+      const uint64_t dD[4] = {64, static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.n / 64),
+                              static_cast<uint64_t>(g.num_groups)};
+      const uint64_t sD4[3] = {sD[0], 128, sD[1]};
+      const uint32_t bD[4] = {64, 32, static_cast<uint32_t>(bn / 128), 1};
+      if (!encode_bf16(&tD, g.d, 4, dD, sD4, bD, CU_TENSOR_MAP_SWIZZLE_128B)) return MGF_ERR_CUDA;
+    } else {
+      // dW [E, m, n] for the epilogue's TMA tile stores: 32 x 32 boxes, 64-byte swizzle
+      const uint64_t dD[3] = {static_cast<uint64_t>(g.n), static_cast<uint64_t>(g.m), static_cast<uint64_t>(g.num_groups)};
+      const uint32_t bD[3] = {32, 32, 1};
+      if (!encode_bf16(&tD, g.d, 3, dD, sD, bD, CU_TENSOR_MAP_SWIZZLE_64B)) return MGF_ERR_CUDA;
+    }
   }
 
   int sms = di.sms - (g.sm_carveout > 0 ? g.sm_carveout : 0);

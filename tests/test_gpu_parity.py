@@ -296,3 +296,32 @@ def test_backward_range_launches_equal_one_launch():
     torch.cuda.synchronize()
     assert torch.equal(dw, dw_ref) and torch.equal(db, db_ref.to(db.dtype))
     assert torch.equal(ga, ga_ref)
+
+
+@pytest.mark.parametrize("m,n,counts", [
+    (256, 128, [300, 0, 517, 41, 600, 1]),   # average above the small-K threshold
+    (136, 80, [70, 0, 131, 5]),              # m and n tails, the ones row inside the last tile
+    (128, 64, [129, 255, 0]),                # m % 128 == 0: the ones row in a tile of its own
+    (384, 256, [1, 7, 129, 0, 64, 33, 200]),
+    (200, 2240, [50, 0, 130, 7]),            # BN = 256, last n tile 192 wide: a warp half of one 64-col chunk
+    (72, 448, [3, 260, 0, 64]),              # BN = 128, last n tile 64 wide; m tail inside a warp's rows
+])
+def test_wgrad_staging_forms_equal(m, n, counts, monkeypatch):
+    """The ragged-K weight + bias gradient stored as 32 x 32 chunks and in the wide small-K form
+    (one TMA store of all a warp's chunks per tile) give the same bits, and match the oracle."""
+    _lib()
+    g = torch.Generator().manual_seed(m + n)
+    rows = sum(counts)
+    a = torch.randn(rows, m, generator=g).to(torch.bfloat16)
+    b = torch.randn(rows, n, generator=g).to(torch.bfloat16)
+    offs = torch.tensor(counts).cumsum(0).to(torch.int32)
+    out = {}
+    for form in ("0", "1"):
+        monkeypatch.setenv("MGF_WGRAD_SMALL_K", form)
+        dw, db = torch.ops.grouped_mm.mm_wgrad_bias(a.cuda().t(), b.cuda(), offs.cuda())
+        torch.cuda.synchronize()
+        out[form] = (dw.cpu(), db.cpu())
+    assert torch.equal(out["0"][0], out["1"][0]) and torch.equal(out["0"][1], out["1"][1])
+    ref_dw, ref_db = O.grouped_wgrad(a, b, offs)
+    _assert_close("dw", out["1"][0], ref_dw)
+    _assert_close("db", out["1"][1], ref_db)
