@@ -658,11 +658,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
         }
         ptx::tc_fence_after();
+        // MMAs of this stage: all of them, except in the short-group form (OB = 4), whose tail
+        // stage stops at the instruction holding the group's last token row, so that only the
+        // rows up to that instruction's end need clearing.
+        int n_mma = kMmaPerStage;
         if constexpr (RAGGED_K) {
           const int valid_k = min(KR, ti.k_end - (ti.k_start + kb * KR));
-          if (valid_k < KR || ones_local >= 0) {
-            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, KR, ones_local, lane);
-            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, KR, ones_local, lane);
+          int end_k = KR;
+          if constexpr (OB == 4) {
+            n_mma = (valid_k + KMMA - 1) / KMMA;
+            end_k = n_mma * KMMA;
+          }
+          if (valid_k < end_k || ones_local >= 0) {
+            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, end_k, ones_local, lane);
+            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -674,6 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = ptx::make_smem_desc_sw128(sB, b_lbo, 1024);
 #pragma unroll
           for (int kk = 0; kk < kMmaPerStage; ++kk) {
+            if (OB == 4 && kk >= n_mma) break;
             // one instruction consumes 32 bytes of every K-major row: K = 16 bf16 or K = 32 e4m3
             if constexpr (CG == 2 && F8) {
               ptx::umma_f8_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
