@@ -94,8 +94,8 @@ def load_peaks():
 
 
 def load_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
-    p = REPO / "profiles" / "dominant_kernel_traffic.json"
+    """Per-launch DRAM bytes of each launch of the step from the committed ncu summary, if any."""
+    p = REPO / "profiles" / "launch_traffic_cfg3.json"
     if p.exists():
         try:
             return json.loads(p.read_text())
@@ -516,13 +516,15 @@ def roofline_entry(ops, local_rows, H, I, peaks, peak_src, fp8=False, steps=None
     if fp8:  # no measured e4m3 peak on this pool: the nominal dense figure
         peak, peak_name = 4500.0, "nominal e4m3 dense 4.5 PFLOP/s (no measured fp8 peak)"
     traffic = load_traffic()
-    tr = None
-    if traffic and traffic.get("op") == name:
-        tr = traffic.get("bytes_per_launch")
+    entry = ((traffic or {}).get("ops") or {}).get(name) if not fp8 else None
+    tr = entry.get("bytes_per_launch") if entry else None
     return {"bound": "tensor", "kernel": name, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
             "frac": ach / peak, "peak_source": peak_name,
             "frac_of_sustained": ach / peaks["bf16_tflops_sustained"],
-            "traffic": tr, "traffic_source": (traffic or {}).get("how") if tr else None,
+            "traffic": tr,
+            "traffic_source": (f"{traffic['what']}; this launch: {entry['captured_read_bytes'] / 1e6:.0f} MB read + "
+                               f"{entry['captured_write_bytes'] / 1e6:.0f} MB written = {entry['ratio_to_algorithmic']}x "
+                               f"its algorithmic bytes {entry['algorithmic_formula']}") if tr else None,
             "algorithmic_flop_per_launch": fl,
             "ops": {k: {"avg_ms": round(v["avg_ms"], 4), "launches": v["launches"],
                         "ms_per_step": round(per_step_ms(v), 4),

@@ -57,9 +57,10 @@ constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
 // 32 x 32 store per chunk.  OB = 4 (short groups): a warp stages all its chunks of a tile (32 rows x
 // up to 128 columns) and stores them with one TMA store, 4x fewer store operations per tile, at the
 // price of a pipeline stage that tiles of a few K stages do not need.
-template <int BN, int CG, bool B_MN, int OB = 1>
+// MH: 128-row accumulators per CTA (2: the 256-row single-CTA weight gradient, both TMEM halves).
+template <int BN, int CG, bool B_MN, int OB = 1, int MH = 1>
 struct TileCfg {
-  static constexpr int A_BYTES = BM * BK * 2;                        // this CTA's 128 rows of A
+  static constexpr int A_BYTES = BM * BK * 2 * MH;                   // this CTA's 128 (or 256) rows of A
   static constexpr int BNC = BN / CG;                                // this CTA's columns of B
   static constexpr int B_CHUNKS = (BNC + 63) / 64;                   // 64-column chunks (MN-major / ragged-K)
   static constexpr int B_BYTES = B_MN ? B_CHUNKS * 8192 : BNC * BK * 2;
@@ -111,6 +112,7 @@ struct Params {
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
   int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
   int small_k;              // ragged-K bf16, single CTAs: one wide TMA store per warp and tile, one stage fewer
+  int m256;                 // ragged-K bf16, single CTAs, BN 256: 256-row tiles (two accumulators share B)
 };
 
 struct TileInfo {
@@ -356,11 +358,13 @@ __device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k
 // Stages whose odd-CTA half must be patched first (ragged-K tails, the ones row) are "relayed":
 // the odd CTA counts their bytes on its own barrier, patches, then arrives on the even CTA's
 // patch_done barrier; every other stage counts both CTAs' bytes directly on the even CTA's barrier.
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1, int MH = 1>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const Params p) {
-  using Cfg = TileCfg<BN, CG, B_MN, OB>;
+  using Cfg = TileCfg<BN, CG, B_MN, OB, MH>;
+  static_assert(MH == 1 || (EPI == MGF_EPI_WGRAD && CG == 1 && !F8 && OB == 1 && BN == 256),
+                "256-row tiles: bf16 single-CTA weight gradient, BN = 256");
   static_assert(OB == 1 || (EPI == MGF_EPI_WGRAD && OB == 4 && CG == 1 && !F8 && BN != 192),
                 "wide output staging: bf16 single-CTA weight gradient, 64-column-aligned warp halves");
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
@@ -370,7 +374,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(!RAGGED_K || KR / KMMA == kMmaPerStage, "ragged-K stage depth");
   static_assert(!(RAGGED_K && F8) || (CG == 1 && (BN == 128 || BN == 256)), "e4m3 weight gradient: single CTA");
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int TM = BM * CG;   // rows of a tile
+  constexpr int MMA_M = BM * CG;  // rows of one MMA (both CTAs of a pair)
+  constexpr int TM = MMA_M * MH;  // rows of a tile
   constexpr int BNC = BN / CG;  // B columns held by one CTA
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -552,10 +557,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kr = ti.k_start + kb * BK;
             const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
             if (p.a_chunked) {
-              load3(sA, &tmA, 0, kr, m0 >> 6);
+#pragma unroll
+              for (int h = 0; h < MH; ++h) load3(sA + h * (BM / 64) * 8192, &tmA, 0, kr, (m0 + h * BM) >> 6);
             } else {
 #pragma unroll
-              for (int c = 0; c < BM / 64; ++c) load2(sA + c * 8192, &tmA, m0 + 64 * c, kr);
+              for (int c = 0; c < MH * BM / 64; ++c) load2(sA + c * 8192, &tmA, m0 + 64 * c, kr);
             }
             if (p.b_chunked) {
               load3(sB, &tmB, 0, kr, nb0 >> 6);
@@ -585,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ UMMA issuer (even CTA) /
     //                                                              ragged-K stage patcher (odd CTA)
     constexpr uint32_t idesc =
-        F8 ? ptx::make_idesc_e4m3(TM, BN, A_MN, B_MN) : ptx::make_idesc_bf16(TM, BN, A_MN, B_MN);
+        F8 ? ptx::make_idesc_e4m3(MMA_M, BN, A_MN, B_MN) : ptx::make_idesc_bf16(MMA_M, BN, A_MN, B_MN);
     // MN-major operands: chunks of 128 bytes along M / N are 8 KB apart (bf16: 64 K rows per chunk)
     // or 16 KB apart (e4m3 weight gradient: 128 K rows); one instruction advances 16 (bf16) or 32
     // (e4m3) K rows of 128 bytes.  K-major: 16-byte units, 32 bytes of K per instruction.
@@ -613,8 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       TileInfo ti;
       decode_tile<TM, RAGGED_K>(t, p, ss, ti);
       const bool odd_ones = odd_has_ones(ti);
-      const int buf = it & 1;
-      const uint32_t tph = (it >> 1) & 1;
+      // two TMEM accumulators in turn; a 256-row tile (MH = 2) fills both, one tile at a time
+      const int buf = MH == 2 ? 0 : (it & 1);
+      const uint32_t tph = MH == 2 ? (it & 1) : ((it >> 1) & 1);
+      // MH = 2: the second 128-row half is multiplied only if it holds rows of dW or the ones row
+      const bool hi_half = MH == 2 && ti.m_blk * TM + BM < p.m + (p.bias_grad ? 1 : 0);
       if (issuer) {
         ok = __all_sync(0xffffffffu,
                         wait_bounded<CG == 2>(ptx::smem_u32(&tempty_bar[buf]), tph ^ 1, abort_flag));
@@ -626,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (RAGGED_K) {
         if (p.bias_grad) {
           const int o = p.m - ti.m_blk * TM - static_cast<int>(crank) * BM;
-          if (o >= 0 && o < BM) ones_local = o;
+          if (o >= 0 && o < BM * MH) ones_local = o;
         }
       }
       for (int kb = 0; kb < ti.nk; ++kb) {
@@ -671,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (valid_k < end_k || ones_local >= 0) {
             if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, end_k, ones_local, lane);
-            else patch_ragged_k_stage<BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
+            else patch_ragged_k_stage<MH * BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
           __syncwarp();
@@ -693,6 +702,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               ptx::umma_f8(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             } else {
               ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+              if (MH == 2 && hi_half)  // rows 128..255: A half two chunks on, accumulator BN columns on
+                ptx::umma_bf16(d_tmem + BN, ptx::make_smem_desc_sw128(sA + (BM / 64) * 8192, a_lbo, 1024) + kk * a_kstep,
+                               bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             }
           }
           if constexpr (CG == 2) ptx::umma_commit_pair(ptx::smem_u32(&empty_bar[stage]), 0x3);
@@ -742,8 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t < 0) break;
       TileInfo ti;
       decode_tile<TM, RAGGED_K>(t, p, ss, ti);
-      const int buf = it & 1;
-      const uint32_t tph = (it >> 1) & 1;
+      const int buf = MH == 2 ? 0 : (it & 1);
+      const uint32_t tph = MH == 2 ? (it & 1) : ((it >> 1) & 1);
       const int n0 = ti.n_blk * BN;
 
       if constexpr (!RAGGED_K) {
@@ -887,124 +899,128 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         if (!__all_sync(0xffffffffu, wait_bounded(ptx::smem_u32(&tfull_bar[buf]), tph, abort_flag))) break;
         ptx::tc_fence_after();
-        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-        // ragged-K weight gradient: rows are output features m0 + r.  dW [E, m, n] is dense, so each
-        // warp stages its 32 rows x 32 columns in its own shared-memory slice and lane 0 stores it
-        // with one TMA tile store (clipped at m and n by the tensor map); no cross-warp sync.
-        const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM;
-        int ones_r = -1;
-        if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
-        const bool row_bias = (r == ones_r);
-        const bool warp_rows = m0 + q * 32 < p.m;  // this warp holds rows of dW
-        const bool warp_active = warp_rows || (ones_r >= q * 32 && ones_r < q * 32 + 32);
-        uint8_t* const slices = out_stage + (warp - 2) * OB * (32 * 64);
-        if (OB == 4 && warp_active) {
-          // wide form: the TMEM loads of two chunks are issued before one wait; the chunks go into
-          // one slab {64 columns, 32 rows, 64-column chunks} (128-byte swizzle: chunk j is 64-column
-          // chunk j / 2, 16-byte units 4 * (j % 2) + g, each at unit ^ (row & 7) within its row's
-          // 128 bytes) and out with one TMA store
-          if (warp_rows) {
-            if (lane == 0) ptx::bulk_wait_read_all();  // the previous tile's store has read the slab
-            __syncwarp();
-          }
-#pragma unroll
-          for (int jb = 0; jb < kChunks; jb += 2) {
-            if (n0 + (c_begin + jb) * 32 >= p.n) break;
-            uint32_t v[2][32];
-            if (ti.nk > 0) {
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-                if (jb + u < kChunks && n0 + (c_begin + jb + u) * 32 < p.n)
-                  ptx::tmem_ld_32x32b_x32(tbase + (c_begin + jb + u) * 32, v[u]);
-              ptx::tmem_ld_wait();
+        // one pass per 128-row accumulator (MH = 2: rows 128..255 sit BN TMEM columns on)
+        for (int h = 0; h < MH; ++h) {
+          const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (buf + h) * BN;
+          // ragged-K weight gradient: rows are output features m0 + r.  dW [E, m, n] is dense, so each
+          // warp stages its 32 rows x 32 columns in its own shared-memory slice and lane 0 stores it
+          // with one TMA tile store (clipped at m and n by the tensor map); no cross-warp sync.
+          const int m0 = ti.m_blk * TM + static_cast<int>(crank) * BM + h * BM;
+          if (h > 0 && m0 >= p.m + (p.bias_grad ? 1 : 0)) break;  // MH = 2: an empty second half
+          int ones_r = -1;
+          if (p.bias_grad && p.m - m0 >= 0 && p.m - m0 < BM) ones_r = p.m - m0;
+          const bool row_bias = (r == ones_r);
+          const bool warp_rows = m0 + q * 32 < p.m;  // this warp holds rows of dW
+          const bool warp_active = warp_rows || (ones_r >= q * 32 && ones_r < q * 32 + 32);
+          uint8_t* const slices = out_stage + (warp - 2) * OB * (32 * 64);
+          if (OB == 4 && warp_active) {
+            // wide form: the TMEM loads of two chunks are issued before one wait; the chunks go into
+            // one slab {64 columns, 32 rows, 64-column chunks} (128-byte swizzle: chunk j is 64-column
+            // chunk j / 2, 16-byte units 4 * (j % 2) + g, each at unit ^ (row & 7) within its row's
+            // 128 bytes) and out with one TMA store
+            if (warp_rows) {
+              if (lane == 0) ptx::bulk_wait_read_all();  // the previous tile's store has read the slab
+              __syncwarp();
             }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int j = jb + u;
-              const int col0 = n0 + (c_begin + j) * 32;
-              if (j >= kChunks || col0 >= p.n) break;
+  #pragma unroll
+            for (int jb = 0; jb < kChunks; jb += 2) {
+              if (n0 + (c_begin + jb) * 32 >= p.n) break;
+              uint32_t v[2][32];
+              if (ti.nk > 0) {
+  #pragma unroll
+                for (int u = 0; u < 2; ++u)
+                  if (jb + u < kChunks && n0 + (c_begin + jb + u) * 32 < p.n)
+                    ptx::tmem_ld_32x32b_x32(tbase + (c_begin + jb + u) * 32, v[u]);
+                ptx::tmem_ld_wait();
+              }
+  #pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int j = jb + u;
+                const int col0 = n0 + (c_begin + j) * 32;
+                if (j >= kChunks || col0 >= p.n) break;
+                uint32_t packed[16];
+  #pragma unroll
+                for (int h = 0; h < 16; ++h)
+                  packed[h] = ti.nk > 0 ? pack_bf16x2(__uint_as_float(v[u][2 * h]), __uint_as_float(v[u][2 * h + 1])) : 0u;
+                if (warp_rows) {
+                  uint8_t* row_base = slices + (j >> 1) * 4096 + lane * 128;
+  #pragma unroll
+                  for (int g = 0; g < 4; ++g)
+                    *reinterpret_cast<uint4*>(row_base + (((4 * (j & 1) + g) ^ (lane & 7)) << 4)) =
+                        make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+                }
+                if (row_bias) {
+                  uint4* dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
+  #pragma unroll
+                  for (int g = 0; g < 4; ++g)
+                    if (col0 + 8 * g < p.n)
+                      dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+                }
+              }
+            }
+            // one store of the warp's chunks (clipped at m, and at the last 64-column chunk of n)
+            const int col_first = n0 + c_begin * 32;
+            if (warp_rows && col_first < p.n) {
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                ptx::tma_store_4d(&tmD, ptx::smem_u32(slices), 0, m0 + q * 32, col_first / 64, ti.e);
+                ptx::bulk_commit();
+              }
+            }
+          } else if (warp_active) {
+  #pragma unroll 1
+            for (int c = c_begin; c < c_begin + kChunks; ++c) {
+              const int col0 = n0 + c * 32;
+              if (col0 >= p.n) break;
               uint32_t packed[16];
-#pragma unroll
-              for (int h = 0; h < 16; ++h)
-                packed[h] = ti.nk > 0 ? pack_bf16x2(__uint_as_float(v[u][2 * h]), __uint_as_float(v[u][2 * h + 1])) : 0u;
+              if (ti.nk > 0) {
+                uint32_t v[32];
+                ptx::tmem_ld_32x32b_x32(tbase + c * 32, v);
+                ptx::tmem_ld_wait();
+                if constexpr (F8) {
+                  // per-feature scales: scale_a of this row's feature (1 for the bias-gradient row),
+                  // scale_b of each column
+                  const float rs = row_bias ? 1.0f : (m0 + r < p.m ? __ldg(p.scale_a + m0 + r) : 0.0f);
+                  const float4* sp = reinterpret_cast<const float4*>(p.scale_b + col0);
+  #pragma unroll
+                  for (int g = 0; g < 8; ++g) {
+                    const float4 sb = (col0 + 4 * g < p.n) ? __ldg(sp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) * (rs * sb.x));
+                    v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) * (rs * sb.y));
+                    v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) * (rs * sb.z));
+                    v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) * (rs * sb.w));
+                  }
+                }
+  #pragma unroll
+                for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(__uint_as_float(v[2 * h]), __uint_as_float(v[2 * h + 1]));
+              } else {
+  #pragma unroll
+                for (int h = 0; h < 16; ++h) packed[h] = 0u;
+              }
               if (warp_rows) {
-                uint8_t* row_base = slices + (j >> 1) * 4096 + lane * 128;
-#pragma unroll
+                const uint32_t slice_u32 = ptx::smem_u32(slices);
+                if (lane == 0) ptx::bulk_wait_read_all();  // the slice's previous store has read it
+                __syncwarp();
+                // 64-byte swizzle (matches the tensor map): 16-byte unit g of row `lane` at g ^ ((lane >> 1) & 3)
+  #pragma unroll
                 for (int g = 0; g < 4; ++g)
-                  *reinterpret_cast<uint4*>(row_base + (((4 * (j & 1) + g) ^ (lane & 7)) << 4)) =
+                  *reinterpret_cast<uint4*>(slices + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
                       make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  ptx::tma_store_3d(&tmD, slice_u32, col0, m0 + q * 32, ti.e);
+                  ptx::bulk_commit();
+                }
               }
               if (row_bias) {
                 uint4* dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
-#pragma unroll
+  #pragma unroll
                 for (int g = 0; g < 4; ++g)
                   if (col0 + 8 * g < p.n)
                     dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
               }
-            }
-          }
-          // one store of the warp's chunks (clipped at m, and at the last 64-column chunk of n)
-          const int col_first = n0 + c_begin * 32;
-          if (warp_rows && col_first < p.n) {
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              ptx::tma_store_4d(&tmD, ptx::smem_u32(slices), 0, m0 + q * 32, col_first / 64, ti.e);
-              ptx::bulk_commit();
-            }
-          }
-        } else if (warp_active) {
-#pragma unroll 1
-          for (int c = c_begin; c < c_begin + kChunks; ++c) {
-            const int col0 = n0 + c * 32;
-            if (col0 >= p.n) break;
-            uint32_t packed[16];
-            if (ti.nk > 0) {
-              uint32_t v[32];
-              ptx::tmem_ld_32x32b_x32(tbase + c * 32, v);
-              ptx::tmem_ld_wait();
-              if constexpr (F8) {
-                // per-feature scales: scale_a of this row's feature (1 for the bias-gradient row),
-                // scale_b of each column
-                const float rs = row_bias ? 1.0f : (m0 + r < p.m ? __ldg(p.scale_a + m0 + r) : 0.0f);
-                const float4* sp = reinterpret_cast<const float4*>(p.scale_b + col0);
-#pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                  const float4 sb = (col0 + 4 * g < p.n) ? __ldg(sp + g) : make_float4(0.f, 0.f, 0.f, 0.f);
-                  v[4 * g] = __float_as_uint(__uint_as_float(v[4 * g]) * (rs * sb.x));
-                  v[4 * g + 1] = __float_as_uint(__uint_as_float(v[4 * g + 1]) * (rs * sb.y));
-                  v[4 * g + 2] = __float_as_uint(__uint_as_float(v[4 * g + 2]) * (rs * sb.z));
-                  v[4 * g + 3] = __float_as_uint(__uint_as_float(v[4 * g + 3]) * (rs * sb.w));
-                }
-              }
-#pragma unroll
-              for (int h = 0; h < 16; ++h) packed[h] = pack_bf16x2(__uint_as_float(v[2 * h]), __uint_as_float(v[2 * h + 1]));
-            } else {
-#pragma unroll
-              for (int h = 0; h < 16; ++h) packed[h] = 0u;
-            }
-            if (warp_rows) {
-              const uint32_t slice_u32 = ptx::smem_u32(slices);
-              if (lane == 0) ptx::bulk_wait_read_all();  // the slice's previous store has read it
-              __syncwarp();
-              // 64-byte swizzle (matches the tensor map): 16-byte unit g of row `lane` at g ^ ((lane >> 1) & 3)
-#pragma unroll
-              for (int g = 0; g < 4; ++g)
-                *reinterpret_cast<uint4*>(slices + lane * 64 + ((g ^ ((lane >> 1) & 3)) << 4)) =
-                    make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
-              ptx::fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                ptx::tma_store_3d(&tmD, slice_u32, col0, m0 + q * 32, ti.e);
-                ptx::bulk_commit();
-              }
-            }
-            if (row_bias) {
-              uint4* dp = reinterpret_cast<uint4*>(p.d2 + (int64_t)ti.e * p.ldd2 + col0);
-#pragma unroll
-              for (int g = 0; g < 4; ++g)
-                if (col0 + 8 * g < p.n)
-                  dp[g] = make_uint4(packed[4 * g], packed[4 * g + 1], packed[4 * g + 2], packed[4 * g + 3]);
             }
           }
         }
@@ -1108,12 +1124,12 @@ static bool debug_sync() {
   return v == 1;
 }
 
-template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1>
+template <int BN, int EPI, bool A_MN, bool B_MN, int CG, bool F8 = false, int OB = 1, int MH = 1>
 static int launch_inst(const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tD, const Params& p,
                        int grid_in, cudaStream_t st) {
   int grid = grid_in;
-  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG, F8, OB>;
-  constexpr int smem = TileCfg<BN, CG, B_MN, OB>::SMEM_BYTES;
+  auto kern = grouped_gemm_kernel<BN, EPI, A_MN, B_MN, CG, F8, OB, MH>;
+  constexpr int smem = TileCfg<BN, CG, B_MN, OB, MH>::SMEM_BYTES;
   static std::mutex mu;
   static bool attr_done[64] = {};
   static int max_clusters[64] = {};
@@ -1206,6 +1222,8 @@ static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, cons
     case MGF_EPI_WGRAD:
       if constexpr (CG == 1 && BN != 192)
         if (p.small_k) return launch_inst<BN, MGF_EPI_WGRAD, true, true, 1, false, 4>(tA, tB, tD, p, grid, st);
+      if constexpr (CG == 1 && BN == 256)
+        if (p.m256) return launch_inst<256, MGF_EPI_WGRAD, true, true, 1, false, 1, 2>(tA, tB, tD, p, grid, st);
       return launch_inst<BN, MGF_EPI_WGRAD, true, true, CG>(tA, tB, tD, p, grid, st);
     default:
       return MGF_ERR_INVALID_ARGUMENT;
@@ -1447,7 +1465,23 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     n_tiles = static_cast<int>((g.n + bn - 1) / bn);
     p.n_tiles = n_tiles;
     cg = f8 ? 1 : pick_cta_group(true, g.total_rows, g.num_groups, g.m);
-    const int tm = BM * cg;
+    // Short groups (a few K stages per tile): the tile time is its dW store epilogue, so each warp
+    // stores its 32 rows x BN/2 columns with one TMA store (the wide form; n a multiple of 64 so
+    // that 64-column chunks never cross a row end).  MGF_WGRAD_SMALL_K=0|1 forces the choice.
+    if (!f8 && cg == 1 && bn != 192 && (g.n % 64) == 0) {
+      const char* env = getenv("MGF_WGRAD_SMALL_K");
+      if (env != nullptr && (env[0] == '0' || env[0] == '1')) p.small_k = env[0] - '0';
+      else p.small_k = (g.total_rows / g.num_groups <= kSmallKTokens) ? 1 : 0;
+    }
+    // Longer groups, BN = 256, single CTAs, m > 128: 256-row tiles, two 128-row accumulators over
+    // all of TMEM sharing each B stage -- a third fewer operand bytes per output at the price of
+    // the TMEM double buffer (measured on cfg3: up / down wgrad 2.86 / 1.50 -> 2.56 / 1.32 ms).
+    // MGF_WGRAD_M256=0|1 forces the choice.
+    if (!f8 && cg == 1 && bn == 256 && !p.small_k) {
+      const char* env = getenv("MGF_WGRAD_M256");
+      p.m256 = (env != nullptr && (env[0] == '0' || env[0] == '1')) ? env[0] - '0' : (g.m > BM ? 1 : 0);
+    }
+    const int tm = BM * cg * (p.m256 ? 2 : 1);
     p.m_tiles_real = static_cast<int>((g.m + tm - 1) / tm);
     p.bias_grad = g.d2 != nullptr ? 1 : 0;
     p.m_tiles = p.m_tiles_real + ((p.bias_grad && (g.m % tm) == 0) ? 1 : 0);
@@ -1499,14 +1533,6 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
       if (!encode_bf16(&tA, g.d, 2, dz, sz, box) || !encode_bf16(&tB, g.d, 2, dz, sz, box)) return MGF_ERR_CUDA;
     }
     tiles_upper = static_cast<int64_t>(p.m_tiles) * n_tiles * g.num_groups;
-    // Short groups (a few K stages per tile): the tile time is its dW store epilogue, so each warp
-    // stores its 32 rows x BN/2 columns with one TMA store (the wide form; n a multiple of 64 so
-    // that 64-column chunks never cross a row end).  MGF_WGRAD_SMALL_K=0|1 forces the choice.
-    if (!f8 && cg == 1 && bn != 192 && (g.n % 64) == 0) {
-      const char* env = getenv("MGF_WGRAD_SMALL_K");
-      if (env != nullptr && (env[0] == '0' || env[0] == '1')) p.small_k = env[0] - '0';
-      else p.small_k = (g.total_rows / g.num_groups <= kSmallKTokens) ? 1 : 0;
-    }
     const uint64_t sD[2] = {static_cast<uint64_t>(g.ldd) * 2, static_cast<uint64_t>(g.ldd_batch) * 2};
     if (p.small_k) {
       // dW as {64 columns, m rows, n / 64 chunks, E}: boxes {64, 32, BN / 128, 1}, 128-byte swizzle

@@ -325,3 +325,31 @@ def test_wgrad_staging_forms_equal(m, n, counts, monkeypatch):
     ref_dw, ref_db = O.grouped_wgrad(a, b, offs)
     _assert_close("dw", out["1"][0], ref_dw)
     _assert_close("db", out["1"][1], ref_db)
+
+
+@pytest.mark.parametrize("m,n,counts", [
+    (2880, 2880, [300, 0, 517, 1000]),   # last 256-row tile holds 64 rows + the ones row: upper half skipped
+    (384, 512, [700, 0, 900]),           # the ones row opens the upper half of the last tile
+    (512, 256, [400, 300]),              # m % 256 == 0: the bias-gradient row in a tile of its own
+    (200, 2304, [333, 290, 0, 411]),     # one tile, both halves partly filled
+])
+def test_wgrad_256_row_tiles_equal_128_row_tiles(m, n, counts, monkeypatch):
+    """The weight + bias gradient with 256-row single-CTA tiles (two accumulators sharing each B
+    stage) gives the same bits as 128-row tiles, and matches the oracle."""
+    _lib()
+    g = torch.Generator().manual_seed(m * 3 + n)
+    rows = sum(counts)
+    a = torch.randn(rows, m, generator=g).to(torch.bfloat16)
+    b = torch.randn(rows, n, generator=g).to(torch.bfloat16)
+    offs = torch.tensor(counts).cumsum(0).to(torch.int32)
+    monkeypatch.setenv("MGF_CTA_GROUP", "1")
+    out = {}
+    for form in ("0", "1"):
+        monkeypatch.setenv("MGF_WGRAD_M256", form)
+        dw, db = torch.ops.grouped_mm.mm_wgrad_bias(a.cuda().t(), b.cuda(), offs.cuda())
+        torch.cuda.synchronize()
+        out[form] = (dw.cpu(), db.cpu())
+    assert torch.equal(out["0"][0], out["1"][0]) and torch.equal(out["0"][1], out["1"][1])
+    ref_dw, ref_db = O.grouped_wgrad(a, b, offs)
+    _assert_close("dw", out["1"][0], ref_dw)
+    _assert_close("db", out["1"][1], ref_db)
