@@ -112,7 +112,7 @@ struct Params {
   const long long* d_rows;  // BIAS scatter mode: destination address of every output row (0 = none)
   int group_begin;          // ragged-M: groups below this index have no tiles (their rows are not touched)
   int small_k;              // ragged-K bf16, single CTAs: one wide TMA store per warp and tile, one stage fewer
-  int m256;                 // ragged-K bf16, single CTAs, BN 256: 256-row tiles (two accumulators share B)
+  int m256;                 // ragged-K single CTAs, BN 256: 256-row tiles (two accumulators share B)
 };
 
 struct TileInfo {
@@ -343,10 +343,10 @@ __device__ __forceinline__ void patch_ragged_k_stage_f8(uint8_t* sA, int valid_k
 #pragma unroll
     for (int c = 0; c < CHUNKS; ++c) *reinterpret_cast<uint4*>(sA + c * 16384 + u * 16) = make_uint4(0, 0, 0, 0);
   }
-  if (ones_local >= 0) {  // A holds 128 features: one chunk; 128-byte swizzle: 16-byte unit ^= row % 8
+  if (ones_local >= 0) {  // A chunks hold 128 features each; 128-byte swizzle: 16-byte unit ^= row % 8
     const int mm = ones_local & 127;
     for (int kr = lane; kr < valid_k; kr += 32) {
-      const int off = kr * 128 + ((((mm >> 4) ^ (kr & 7))) << 4) + (mm & 15);
+      const int off = (ones_local >> 7) * 16384 + kr * 128 + ((((mm >> 4) ^ (kr & 7))) << 4) + (mm & 15);
       sA[off] = 0x38u;
     }
   }
@@ -363,8 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const Params p) {
   using Cfg = TileCfg<BN, CG, B_MN, OB, MH>;
-  static_assert(MH == 1 || (EPI == MGF_EPI_WGRAD && CG == 1 && !F8 && OB == 1 && BN == 256),
-                "256-row tiles: bf16 single-CTA weight gradient, BN = 256");
+  static_assert(MH == 1 || (EPI == MGF_EPI_WGRAD && CG == 1 && OB == 1 && BN == 256),
+                "256-row tiles: single-CTA weight gradient, BN = 256");
   static_assert(OB == 1 || (EPI == MGF_EPI_WGRAD && OB == 4 && CG == 1 && !F8 && BN != 192),
                 "wide output staging: bf16 single-CTA weight gradient, 64-column-aligned warp halves");
   constexpr bool RAGGED_K = (EPI == MGF_EPI_WGRAD);
@@ -550,7 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // e4m3 token rows: one {128 features, 128 rows} box per 128 columns of A and of B
             const int kr = ti.k_start + kb * KR;
             const int m0 = ti.m_blk * TM;
-            load2(sA, &tmA, m0, kr);
+#pragma unroll
+            for (int h = 0; h < MH; ++h) load2(sA + h * 16384, &tmA, m0 + h * BM, kr);
 #pragma unroll
             for (int c = 0; c < BNC / 128; ++c) load2(sB + c * 16384, &tmB, nb0 + 128 * c, kr);
           } else {
@@ -679,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             end_k = n_mma * KMMA;
           }
           if (valid_k < end_k || ones_local >= 0) {
-            if constexpr (F8) patch_ragged_k_stage_f8<1 + BNC / 128>(sA_ptr, valid_k, end_k, ones_local, lane);
+            if constexpr (F8) patch_ragged_k_stage_f8<MH + BNC / 128>(sA_ptr, valid_k, end_k, ones_local, lane);
             else patch_ragged_k_stage<MH * BM / 64, Cfg::B_CHUNKS>(sA_ptr, valid_k, end_k, ones_local, lane);
             ptx::fence_proxy_async_smem();
           }
@@ -700,6 +701,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               ptx::umma_bf16_pair(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             } else if constexpr (F8) {
               ptx::umma_f8(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
+              if (MH == 2 && hi_half)  // rows 128..255: the second 16 KB A chunk, BN TMEM columns on
+                ptx::umma_f8(d_tmem + BN, ptx::make_smem_desc_sw128(sA + 16384, a_lbo, 1024) + kk * a_kstep,
+                             bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
             } else {
               ptx::umma_bf16(d_tmem, adesc + kk * a_kstep, bdesc + kk * b_kstep, idesc, (kb | kk) != 0 ? 1u : 0u);
               if (MH == 2 && hi_half)  // rows 128..255: A half two chunks on, accumulator BN columns on
@@ -1198,6 +1202,8 @@ static int dispatch_epi(int epi, bool b_mn, bool f8, const CUtensorMap& tA, cons
                         const CUtensorMap& tD, const Params& p, int grid, cudaStream_t st) {
   if (f8) {  // e4m3: ragged-M epilogues with both operands K-major; the ragged-K weight gradient
     if (epi == MGF_EPI_WGRAD) {
+      if constexpr (CG == 1 && BN == 256)
+        if (p.m256) return launch_inst<256, MGF_EPI_WGRAD, true, true, 1, true, 1, 2>(tA, tB, tD, p, grid, st);
       if constexpr (CG == 1 && (BN == 128 || BN == 256))
         return launch_inst<BN, MGF_EPI_WGRAD, true, true, 1, true>(tA, tB, tD, p, grid, st);
       return MGF_ERR_INVALID_ARGUMENT;
@@ -1477,7 +1483,7 @@ extern "C" int mgf_grouped_gemm_launch(const mgf_gemm_desc* desc, void* stream) 
     // all of TMEM sharing each B stage -- a third fewer operand bytes per output at the price of
     // the TMEM double buffer (measured on cfg3: up / down wgrad 2.86 / 1.50 -> 2.56 / 1.32 ms).
     // MGF_WGRAD_M256=0|1 forces the choice.
-    if (!f8 && cg == 1 && bn == 256 && !p.small_k) {
+    if (cg == 1 && bn == 256 && !p.small_k) {
       const char* env = getenv("MGF_WGRAD_M256");
       p.m256 = (env != nullptr && (env[0] == '0' || env[0] == '1')) ? env[0] - '0' : (g.m > BM ? 1 : 0);
     }

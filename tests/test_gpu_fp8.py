@@ -101,9 +101,9 @@ def test_fp8_swiglu_bwd(cg, E, H, I, counts, monkeypatch):
     (256, 256, [300, 7, 0, 129]),               # m % 128 == 0: the ones row gets its own m tile
     (2880, 5760, [1029, 0, 640, 1]),            # GPT-OSS widths
 ])
-def test_fp8_wgrad_bias(m_, n, counts):
+def test_fp8_wgrad_bias(m_, n, counts, monkeypatch):
     """e4m3 ragged-K weight + bias gradient against fp32 on the per-column-dequantised operands;
-    empty groups give exact zeros."""
+    empty groups give exact zeros.  The 128-row and the 256-row single-CTA tiles give the same bits."""
     import cutlass_op.bf16_grouped_mm as m
     from cutlass_op.bf16_grouped_mm import fp8
 
@@ -114,9 +114,14 @@ def test_fp8_wgrad_bias(m_, n, counts):
     offs = torch.cumsum(torch.tensor(counts, dtype=torch.int64), 0).to(torch.int32)
     qa, sa = fp8.quantize_cols(a.cuda())
     qb, sb = fp8.quantize_cols(b.cuda())
-    dw, db = fp8.grouped_mm_wgrad_fp8(qa, qb, offs.cuda(), sa, sb)
-    torch.cuda.synchronize()
-    m.check_device_status()
+    forms = {}
+    for form in ("0", "1"):
+        monkeypatch.setenv("MGF_WGRAD_M256", form)
+        forms[form] = fp8.grouped_mm_wgrad_fp8(qa, qb, offs.cuda(), sa, sb)
+        torch.cuda.synchronize()
+        m.check_device_status()
+    assert torch.equal(forms["0"][0], forms["1"][0]) and torch.equal(forms["0"][1], forms["1"][1])
+    dw, db = forms["1"]
     ad, bd = fp8.dequantize_cols(qa, sa).cpu(), fp8.dequantize_cols(qb, sb).cpu()
     ref_w, ref_b = O.grouped_wgrad(ad, bd, offs)
     for e, (s0, s1) in enumerate(O.segments(offs)):
