@@ -8,7 +8,10 @@
 //            then an elementwise pass;
 //   weights  [E, K, N] (any strides) -> e4m3 [E, N, K] with K contiguous (the K-major B operand) and
 //            one scale per (e, n): the same two passes over 32 x 32 tiles, the second transposing
-//            through shared memory so that both the read and the write are coalesced.
+//            through shared memory so that both the read and the write are coalesced;
+//   weights, both axes  [E, K, N] with unit stride along n -> the K-major codes above AND the codes of
+//            w^T (one scale per (e, k), n contiguous: the dgrad's B operand) from two passes instead of
+//            four: one read for both amax sets, one read for both code sets.
 // These replace chains of eager torch ops (abs, amax, divide, clamp, copy, transpose) that cost more
 // than the e4m3 GEMMs they feed.
 #include <cuda_bf16.h>
@@ -297,6 +300,114 @@ __global__ void __launch_bounds__(256) w_quant_vec_kernel(const __nv_bfloat16* _
   }
 }
 
+// Both-axes amax: a block covers 256 columns (8 per lane) and 128 k rows (16 per warp); per-column
+// maxima over the block's rows and per-row maxima over its columns go out as atomicMax on the fp32
+// bit patterns of |w| (non-negative floats order like their bits).
+__global__ void __launch_bounds__(256) w_amax_both_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                          int64_t s_e, int64_t s_k, unsigned int* __restrict__ amax_n,
+                                                          unsigned int* __restrict__ amax_k) {
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 128;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 256 + lane * 8;
+  const __nv_bfloat16* we = w + e * s_e;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < 16; ++i) {
+    const int64_t k = k0 + wid + 8 * i;  // warp-uniform
+    if (k >= K) break;
+    float rm = 0.0f;
+    if (n0 < N) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(we + k * s_k + n0));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+        m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+        rm = fmaxf(rm, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+    if (lane == 0) atomicMax(amax_k + e * K + k, __float_as_uint(rm));
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[wid][lane * 8 + j] = m[j];
+  __syncthreads();
+  float mm = red[0][threadIdx.x];
+#pragma unroll
+  for (int t = 1; t < 8; ++t) mm = fmaxf(mm, red[t][threadIdx.x]);
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (n < N) atomicMax(amax_n + e * N + n, __float_as_uint(mm));
+}
+
+// Both-axes codes from one 64 (k) x 64 (n) tile in shared memory: q_a[e][n][k] (k contiguous, scale per
+// (e, n)), written as in w_quant_vec_kernel, and q_b[e][k][n] (n contiguous, scale per (e, k)): every
+// thread writes 16 consecutive n codes of one k as one 16-byte store.
+__global__ void __launch_bounds__(256) w_quant_both_kernel(const __nv_bfloat16* __restrict__ w, int64_t K, int64_t N,
+                                                           int64_t s_e, int64_t s_k, const float* __restrict__ sa,
+                                                           uint8_t* __restrict__ qa, int64_t ldqa,
+                                                           const float* __restrict__ sb, uint8_t* __restrict__ qb,
+                                                           int64_t ldqb) {
+  __shared__ float tile[64][65];  // [k][n]
+  const int64_t e = blockIdx.z, k0 = static_cast<int64_t>(blockIdx.y) * 64, n0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const __nv_bfloat16* we = w + e * s_e;
+  for (int it = threadIdx.x; it < 512; it += 256) {  // 64 k lines x 8 vectors of 8 n
+    const int line = it >> 3, vec = it & 7;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int64_t kk = k0 + line, nn = n0 + vec * 8;
+    if (kk < K && nn < N) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(we + kk * s_k + nn));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 v = __bfloat1622float2(h[j]);
+        f[2 * j] = v.x;
+        f[2 * j + 1] = v.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) tile[line][vec * 8 + j] = f[j];
+  }
+  __syncthreads();
+  {  // q_a: 64 n x 4 groups of 16 k
+    const int nl = threadIdx.x >> 2, kq = (threadIdx.x & 3) * 16;
+    const int64_t n = n0 + nl, k = k0 + kq;
+    if (n < N && k < K) {
+      const float s = __ldg(sa + e * N + n);
+      uint32_t wds[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t wv = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) wv |= static_cast<uint32_t>(to_e4m3(tile[kq + 4 * g + b][nl] / s)) << (8 * b);
+        wds[g] = wv;
+      }
+      uint8_t* dst = qa + (e * N + n) * ldqa + k;
+      if (k + 16 <= K) *reinterpret_cast<uint4*>(dst) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+      else for (int i = 0; i < K - k; ++i) dst[i] = static_cast<uint8_t>(wds[i >> 2] >> (8 * (i & 3)));
+    }
+  }
+  {  // q_b: 64 k x 4 groups of 16 n
+    const int kl = threadIdx.x >> 2, nq = (threadIdx.x & 3) * 16;
+    const int64_t k = k0 + kl, n = n0 + nq;
+    if (k < K && n < N) {
+      const float s = __ldg(sb + e * K + k);
+      uint32_t wds[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint32_t wv = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) wv |= static_cast<uint32_t>(to_e4m3(tile[kl][nq + 4 * g + b] / s)) << (8 * b);
+        wds[g] = wv;
+      }
+      uint8_t* dst = qb + (e * K + k) * ldqb + n;
+      if (n + 16 <= N) *reinterpret_cast<uint4*>(dst) = make_uint4(wds[0], wds[1], wds[2], wds[3]);
+      else for (int i = 0; i < N - n; ++i) dst[i] = static_cast<uint8_t>(wds[i >> 2] >> (8 * (i & 3)));
+    }
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -370,6 +481,36 @@ extern "C" int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int
       if (n_fast) w_quant_kernel<true><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
       else w_quant_kernel<false><<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, s_n, scale, static_cast<uint8_t*>(q), ldq);
     }
+  }
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_fp8_quantize_weights_both(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k,
+                                             void* qa, int64_t ldqa, float* sa, void* qb, int64_t ldqb, float* sb,
+                                             void* stream) {
+  using namespace mgf;
+  if (E < 0 || K < 0 || N < 0 || ldqa < K || ldqb < N) return MGF_ERR_INVALID_ARGUMENT;
+  if (E == 0) return MGF_OK;
+  if (w == nullptr || qa == nullptr || qb == nullptr || sa == nullptr || sb == nullptr) return MGF_ERR_INVALID_ARGUMENT;
+  if (!aligned16(w) || N % 8 || s_k % 8 || s_e % 8 || ldqa % 16 || ldqb % 16 || !aligned16(qa) || !aligned16(qb) ||
+      !aligned16(sa) || !aligned16(sb))
+    return MGF_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(sa, 0, sizeof(float) * E * N, st) != cudaSuccess ||
+      cudaMemsetAsync(sb, 0, sizeof(float) * E * K, st) != cudaSuccess)
+    return MGF_ERR_CUDA;
+  const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(w);
+  if (K > 0 && N > 0) {
+    const dim3 agrid(static_cast<unsigned>((N + 255) / 256), static_cast<unsigned>((K + 127) / 128), static_cast<unsigned>(E));
+    w_amax_both_kernel<<<agrid, 256, 0, st>>>(wp, K, N, s_e, s_k, reinterpret_cast<unsigned int*>(sa),
+                                              reinterpret_cast<unsigned int*>(sb));
+  }
+  if (N > 0) amax_to_scale_kernel<<<static_cast<unsigned>((E * N + 255) / 256), 256, 0, st>>>(sa, E * N);
+  if (K > 0) amax_to_scale_kernel<<<static_cast<unsigned>((E * K + 255) / 256), 256, 0, st>>>(sb, E * K);
+  if (K > 0 && N > 0) {
+    const dim3 grid(static_cast<unsigned>((N + 63) / 64), static_cast<unsigned>((K + 63) / 64), static_cast<unsigned>(E));
+    w_quant_both_kernel<<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, sa, static_cast<uint8_t*>(qa), ldqa, sb,
+                                              static_cast<uint8_t*>(qb), ldqb);
   }
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }

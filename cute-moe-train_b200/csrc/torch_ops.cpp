@@ -904,6 +904,24 @@ std::tuple<Tensor, Tensor> fp8_quantize_weights_cuda(const Tensor& w) {
   return {qt.as_strided({E, K, N}, {N * kp, 1, kp}), scale};
 }
 
+// Both quantisations of one weight in two passes (see mgf_fp8_quantize_weights_both): the results of
+// fp8_quantize_weights(w) and of fp8_quantize_weights(w.transpose(-2, -1)).
+std::tuple<Tensor, Tensor, Tensor, Tensor> fp8_quantize_weights_both_cuda(const Tensor& w) {
+  TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == at::kBFloat16 && w.stride(2) == 1,
+              "fp8_quantize_weights_both: w must be a bf16 [E, K, N] CUDA tensor with unit stride along N");
+  const c10::cuda::CUDAGuard guard(w.device());
+  const int64_t E = w.size(0), K = w.size(1), N = w.size(2), kpa = pad16(K), kpb = pad16(N);
+  Tensor qa = at::empty({E, N, kpa}, w.options().dtype(at::kFloat8_e4m3fn));
+  Tensor sa = at::empty({E, N}, w.options().dtype(at::kFloat));
+  Tensor qb = at::empty({E, K, kpb}, w.options().dtype(at::kFloat8_e4m3fn));
+  Tensor sb = at::empty({E, K}, w.options().dtype(at::kFloat));
+  check_launch(mgf_fp8_quantize_weights_both(w.data_ptr(), E, K, N, w.stride(0), w.stride(1), qa.data_ptr(), kpa,
+                                             sa.data_ptr<float>(), qb.data_ptr(), kpb, sb.data_ptr<float>(),
+                                             at::cuda::getCurrentCUDAStream().stream()),
+               "fp8_quantize_weights_both");
+  return {qa.as_strided({E, K, N}, {N * kpa, 1, kpa}), sa, qb.as_strided({E, N, K}, {K * kpb, 1, kpb}), sb};
+}
+
 // Wait on the current stream until every slot of this rank's flag array reaches seq (see mgf_wait_flags).
 void wait_flags_cuda(const Tensor& flags, int64_t seq, int64_t timeout_ns) {
   TORCH_CHECK(flags.is_cuda() && flags.scalar_type() == at::kLong && flags.is_contiguous(),
@@ -965,6 +983,7 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def("fp8_quantize_rows(Tensor x) -> (Tensor, Tensor)");
   m.def("fp8_quantize_cols(Tensor x) -> (Tensor, Tensor)");
   m.def("fp8_quantize_weights(Tensor w) -> (Tensor, Tensor)");
+  m.def("fp8_quantize_weights_both(Tensor w) -> (Tensor, Tensor, Tensor, Tensor)");
   m.def("signal_flags(Tensor flag_bases, int rank, int seq) -> ()");
   m.def("mm_scatter(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor row_ptrs) -> ()");
   m.def("ep_sort(Tensor expert_ids, int num_experts, int topk) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
@@ -995,6 +1014,7 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("fp8_quantize_rows", &fp8_quantize_rows_cuda);
   m.impl("fp8_quantize_cols", &fp8_quantize_cols_cuda);
   m.impl("fp8_quantize_weights", &fp8_quantize_weights_cuda);
+  m.impl("fp8_quantize_weights_both", &fp8_quantize_weights_both_cuda);
   m.impl("signal_flags", &signal_flags_cuda);
   m.impl("mm_scatter", &mm_scatter_cuda);
   m.impl("ep_sort", &ep_sort_cuda);

@@ -102,6 +102,19 @@ def quantize_weights(w: torch.Tensor, native: bool = True) -> tuple[torch.Tensor
     return qt.transpose(1, 2), scale.contiguous()
 
 
+def quantize_weights_both(w: torch.Tensor, native: bool = True):
+    """[E, K, N] -> (quantize_weights(w), quantize_weights(w^T)) as (q, scale, q_t, scale_t): the forward's
+    K-major B operand and the dgrad's, bit-identical to the two calls; with unit stride along N the fused
+    kernel reads w twice instead of four times (grouped_mm::fp8_quantize_weights_both)."""
+    if native and w.is_cuda and w.dtype == torch.bfloat16 and w.stride(2) == 1 and w.shape[2] % 8 == 0 \
+            and w.stride(1) % 8 == 0 and w.stride(0) % 8 == 0 and w.data_ptr() % 16 == 0:
+        with timed("fp8_quantize"):
+            return torch.ops.grouped_mm.fp8_quantize_weights_both(w.detach())
+    q, s = quantize_weights(w, native)
+    q_t, s_t = quantize_weights(w.transpose(-2, -1), native)
+    return q, s, q_t, s_t
+
+
 def quantize_cols(x: torch.Tensor, native: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """[M, K] -> (e4m3 [M, K] with a 16-byte row pitch, fp32 [K] scales): x ~= q * scale[None, :]
     (one scale per feature column over all rows: the weight-gradient operands)."""
@@ -170,18 +183,19 @@ class _FFNFp8(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_up, b_up, w_down, b_down, offs, alpha, limit):
         qx, sx = quantize_rows(x)
-        qwu, swu = quantize_weights(w_up)
+        # both axes of each weight at once: the forward's operand now, the dgrad's kept for backward
+        qwu, swu, qwut, swut = quantize_weights_both(w_up)
         s, aux = grouped_mm_swiglu_fp8(qx, qwu, offs, sx, swu, b_up, alpha, limit)
         qs, ss = quantize_rows(s)
-        qwd, swd = quantize_weights(w_down)
+        qwd, swd, qwdt, swdt = quantize_weights_both(w_down)
         out = grouped_mm_fp8(qs, qwd, offs, ss, swd, b_down)
-        ctx.save_for_backward(x, w_up, w_down, s, aux, offs)
+        ctx.save_for_backward(x, qwut, swut, qwdt, swdt, s, aux, offs)
         ctx.alpha, ctx.limit = alpha, limit
         return out
 
     @staticmethod
     def backward(ctx, g):
-        x, w_up, w_down, s, aux, offs = ctx.saved_tensors
+        x, qwut, swut, qwdt, swdt, s, aux, offs = ctx.saved_tensors
         g = g.contiguous()
         # down-proj weight + bias gradients over token rows (per-column scales)
         qs_c, ss_c = quantize_cols(s)
@@ -189,11 +203,9 @@ class _FFNFp8(torch.autograd.Function):
         g_wd, g_bd = grouped_mm_wgrad_fp8(qs_c, qg_c, offs, ss_c, sg_c)
         # down-proj dgrad + SwiGLU backward (row scales for grad_out, column scales for W_down^T)
         qg, sg = quantize_rows(g)
-        qwdt, swdt = quantize_weights(w_down.transpose(-2, -1))
         grad_aux = grouped_mm_swiglu_bwd_fp8(qg, qwdt, offs, aux, sg, swdt, ctx.alpha, ctx.limit)
         # up-proj dgrad and weight + bias gradients
         qga, sga = quantize_rows(grad_aux)
-        qwut, swut = quantize_weights(w_up.transpose(-2, -1))
         g_x = grouped_mm_fp8(qga, qwut, offs, sga, swut, None)
         qx_c, sx_c = quantize_cols(x)
         qga_c, sga_c = quantize_cols(grad_aux)

@@ -238,6 +238,12 @@ int mgf_fp8_quantize_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx
                           void* stream);
 int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k, int64_t s_n,
                              void* q, int64_t ldq, float* scale, void* stream);
+/* Both axes of one weight [E, K, N] (unit stride along n, n % 8 == 0, 16-byte aligned strides and
+ * bases) in two passes: qa [E, N, ldqa] / sa [E, N] as mgf_fp8_quantize_weights gives for w, and
+ * qb [E, K, ldqb] / sb [E, K] as it gives for w^T (codes n-contiguous, one scale per (e, k));
+ * bit-identical to the two calls (no counterpart in the reference). */
+int mgf_fp8_quantize_weights_both(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k, void* qa,
+                                  int64_t ldqa, float* sa, void* qb, int64_t ldqb, float* sb, void* stream);
 
 /* Map a peer process's device allocation (its 64-byte cudaIpcMemHandle_t) into the context of
  * the calling thread's current device, peer access enabled, for mgf_push_rows destinations

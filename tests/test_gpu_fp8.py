@@ -179,3 +179,21 @@ def test_fused_quantisers_match_the_formula(shape):
             qr, sr = fp8.quantize_weights(ww, native=False)
             assert torch.equal(s, sr)
             assert q.stride(1) == 1 and torch.equal(q.view(torch.uint8), qr.view(torch.uint8))
+
+
+@pytest.mark.parametrize("shape", [(3, 136, 40), (2, 2880, 5760), (4, 70, 264), (1, 1, 8)])
+def test_fused_both_axes_weight_quantiser_matches_two_calls(shape):
+    """quantize_weights_both(w) gives exactly quantize_weights(w) and quantize_weights(w^T): the same
+    codes and scales bit for bit, k and n tails included."""
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    E, K, N = shape
+    g = torch.Generator().manual_seed(E * K + N)
+    w = (torch.randn(E, K, N, generator=g) * torch.linspace(0.01, 4.0, N)).to(torch.bfloat16).cuda()
+    q, s, q_t, s_t = fp8.quantize_weights_both(w)
+    r, rs = fp8.quantize_weights(w)
+    r_t, rs_t = fp8.quantize_weights(w.transpose(-2, -1))
+    torch.cuda.synchronize()
+    assert q.shape == r.shape and q_t.shape == r_t.shape
+    assert torch.equal(q.view(torch.uint8), r.view(torch.uint8)) and torch.equal(s, rs)
+    assert torch.equal(q_t.view(torch.uint8), r_t.view(torch.uint8)) and torch.equal(s_t, rs_t)
