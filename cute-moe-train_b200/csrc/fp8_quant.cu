@@ -9,6 +9,9 @@
 //   weights  [E, K, N] (any strides) -> e4m3 [E, N, K] with K contiguous (the K-major B operand) and
 //            one scale per (e, n): the same two passes over 32 x 32 tiles, the second transposing
 //            through shared memory so that both the read and the write are coalesced;
+//   rows + cols  both scalings of one activation (the backward's grad_out and grad_aux feed a dgrad by
+//            rows and a weight gradient by columns): one read for both amax sets, one read for both
+//            code sets, instead of three;
 //   weights, both axes  [E, K, N] with unit stride along n -> the K-major codes above AND the codes of
 //            w^T (one scale per (e, k), n contiguous: the dgrad's B operand) from two passes instead of
 //            four: one read for both amax sets, one read for both code sets.
@@ -103,6 +106,77 @@ __global__ void __launch_bounds__(256) col_amax_kernel(const __nv_bfloat16* __re
   for (int t = 1; t < 8; ++t) mm = fmaxf(mm, red[t][c]);
   const int64_t col = static_cast<int64_t>(blockIdx.x) * 256 + c;
   if (col < cols) atomicMax(amax + col, __float_as_uint(mm));
+}
+
+// Rows + cols amax: the col_amax_kernel tiling; each warp's row (256 columns of it) is also reduced
+// across the lanes and sent to the row's amax with one atomicMax per row and block.
+__global__ void __launch_bounds__(256) rowcol_amax_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                          int64_t cols, int64_t ldx, unsigned int* __restrict__ amax_c,
+                                                          unsigned int* __restrict__ amax_r) {
+  __shared__ float red[8][256];
+  const int lane = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const int64_t r_begin = static_cast<int64_t>(blockIdx.y) * kRowsPerBlock;
+  const int64_t r_end = r_begin + kRowsPerBlock < rows ? r_begin + kRowsPerBlock : rows;
+  const bool in = v * 8 < cols;
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int64_t r = r_begin + ty; r < r_end; r += 8) {  // warp-uniform
+    float rm = 0.0f;
+    if (in) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        m[2 * j] = fmaxf(m[2 * j], fabsf(f.x));
+        m[2 * j + 1] = fmaxf(m[2 * j + 1], fabsf(f.y));
+        rm = fmaxf(rm, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+    if (lane == 0) atomicMax(amax_r + r, __float_as_uint(rm));
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[ty][lane * 8 + j] = m[j];
+  __syncthreads();
+  const int c = threadIdx.x;
+  float mm = red[0][c];
+#pragma unroll
+  for (int t = 1; t < 8; ++t) mm = fmaxf(mm, red[t][c]);
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * 256 + c;
+  if (col < cols) atomicMax(amax_c + col, __float_as_uint(mm));
+}
+
+// Rows + cols codes: one 8-element vector per thread, both code sets from one read.
+__global__ void __launch_bounds__(256) quant_rows_cols_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                              int64_t cols, int64_t ldx,
+                                                              const float* __restrict__ s_r, uint8_t* __restrict__ q_r,
+                                                              int64_t ldq_r, const float* __restrict__ s_c,
+                                                              uint8_t* __restrict__ q_c, int64_t ldq_c) {
+  const int64_t nv = cols / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * nv) return;
+  const int64_t r = i / nv, v = i - r * nv;
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + v);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float sr = __ldg(s_r + r);
+  const float4 s0 = __ldg(reinterpret_cast<const float4*>(s_c + v * 8));
+  const float4 s1 = __ldg(reinterpret_cast<const float4*>(s_c + v * 8) + 1);
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  uint32_t wr[2], wc[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float2 a = __bfloat1622float2(h[2 * j]);
+    const float2 b = __bfloat1622float2(h[2 * j + 1]);
+    wr[j] = static_cast<uint32_t>(to_e4m3(a.x / sr)) | (static_cast<uint32_t>(to_e4m3(a.y / sr)) << 8) |
+            (static_cast<uint32_t>(to_e4m3(b.x / sr)) << 16) | (static_cast<uint32_t>(to_e4m3(b.y / sr)) << 24);
+    wc[j] = static_cast<uint32_t>(to_e4m3(a.x / sv[4 * j])) | (static_cast<uint32_t>(to_e4m3(a.y / sv[4 * j + 1])) << 8) |
+            (static_cast<uint32_t>(to_e4m3(b.x / sv[4 * j + 2])) << 16) |
+            (static_cast<uint32_t>(to_e4m3(b.y / sv[4 * j + 3])) << 24);
+  }
+  *reinterpret_cast<uint2*>(q_r + r * ldq_r + v * 8) = make_uint2(wr[0], wr[1]);
+  *reinterpret_cast<uint2*>(q_c + r * ldq_c + v * 8) = make_uint2(wc[0], wc[1]);
 }
 
 __global__ void amax_to_scale_kernel(float* __restrict__ s, int64_t n) {  // in place: amax bits -> scale
@@ -511,6 +585,36 @@ extern "C" int mgf_fp8_quantize_weights_both(const void* w, int64_t E, int64_t K
     const dim3 grid(static_cast<unsigned>((N + 63) / 64), static_cast<unsigned>((K + 63) / 64), static_cast<unsigned>(E));
     w_quant_both_kernel<<<grid, 256, 0, st>>>(wp, K, N, s_e, s_k, sa, static_cast<uint8_t*>(qa), ldqa, sb,
                                               static_cast<uint8_t*>(qb), ldqb);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
+}
+
+extern "C" int mgf_fp8_quantize_rows_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q_r,
+                                          int64_t ldq_r, float* s_r, void* q_c, int64_t ldq_c, float* s_c,
+                                          void* stream) {
+  using namespace mgf;
+  if (rows < 0 || cols < 0 || (cols > 0 && s_c == nullptr) || (rows > 0 && (s_r == nullptr)) ||
+      (rows > 0 && cols > 0 && (x == nullptr || q_r == nullptr || q_c == nullptr)))
+    return MGF_ERR_INVALID_ARGUMENT;
+  if (cols % 8 || ldx % 8 || ldq_r % 8 || ldq_c % 8 || (rows > 0 && cols > 0 && !aligned16(x)) ||
+      (cols > 0 && !aligned16(s_c)) || (reinterpret_cast<uintptr_t>(q_r) & 7u) || (reinterpret_cast<uintptr_t>(q_c) & 7u))
+    return MGF_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((cols > 0 && cudaMemsetAsync(s_c, 0, sizeof(float) * cols, st) != cudaSuccess) ||
+      (rows > 0 && cudaMemsetAsync(s_r, 0, sizeof(float) * rows, st) != cudaSuccess))
+    return MGF_ERR_CUDA;
+  if (rows > 0 && cols > 0) {
+    const dim3 grid(static_cast<unsigned>((cols / 8 + 31) / 32), static_cast<unsigned>((rows + kRowsPerBlock - 1) / kRowsPerBlock));
+    rowcol_amax_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, ldx,
+                                             reinterpret_cast<unsigned int*>(s_c), reinterpret_cast<unsigned int*>(s_r));
+  }
+  if (cols > 0) amax_to_scale_kernel<<<static_cast<unsigned>((cols + 255) / 256), 256, 0, st>>>(s_c, cols);
+  if (rows > 0) amax_to_scale_kernel<<<static_cast<unsigned>((rows + 255) / 256), 256, 0, st>>>(s_r, rows);
+  if (rows > 0 && cols > 0) {
+    const int64_t items = rows * (cols / 8);
+    quant_rows_cols_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), rows, cols, ldx, s_r, static_cast<uint8_t*>(q_r), ldq_r, s_c,
+        static_cast<uint8_t*>(q_c), ldq_c);
   }
   return cudaGetLastError() == cudaSuccess ? MGF_OK : MGF_ERR_CUDA;
 }

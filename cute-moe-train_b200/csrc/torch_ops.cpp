@@ -891,6 +891,24 @@ std::tuple<Tensor, Tensor> fp8_quantize_cols_cuda(const Tensor& x) {
   return {q, scale};
 }
 
+// Both scalings of one activation (see mgf_fp8_quantize_rows_cols): fp8_quantize_rows(x) and
+// fp8_quantize_cols(x) from two passes.
+std::tuple<Tensor, Tensor, Tensor, Tensor> fp8_quantize_rows_cols_cuda(const Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1,
+              "fp8_quantize_rows_cols: x must be a row-major bf16 [rows, cols] CUDA tensor");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = x.size(0), cols = x.size(1);
+  Tensor q_r = at::empty_strided({rows, cols}, {pad16(cols), 1}, x.options().dtype(at::kFloat8_e4m3fn));
+  Tensor s_r = at::empty({rows}, x.options().dtype(at::kFloat));
+  Tensor q_c = at::empty_strided({rows, cols}, {pad16(cols), 1}, x.options().dtype(at::kFloat8_e4m3fn));
+  Tensor s_c = at::empty({cols}, x.options().dtype(at::kFloat));
+  check_launch(mgf_fp8_quantize_rows_cols(x.data_ptr(), rows, cols, rows > 0 ? x.stride(0) : 8, q_r.data_ptr(),
+                                          q_r.stride(0), s_r.data_ptr<float>(), q_c.data_ptr(), q_c.stride(0),
+                                          s_c.data_ptr<float>(), at::cuda::getCurrentCUDAStream().stream()),
+               "fp8_quantize_rows_cols");
+  return {q_r, s_r, q_c, s_c};
+}
+
 std::tuple<Tensor, Tensor> fp8_quantize_weights_cuda(const Tensor& w) {
   TORCH_CHECK(w.is_cuda() && w.dim() == 3 && w.scalar_type() == at::kBFloat16 && (w.stride(2) == 1 || w.stride(1) == 1),
               "fp8_quantize_weights: w must be a bf16 [E, K, N] CUDA tensor with unit stride along K or N");
@@ -984,6 +1002,7 @@ TORCH_LIBRARY(grouped_mm, m) {
   m.def("fp8_quantize_cols(Tensor x) -> (Tensor, Tensor)");
   m.def("fp8_quantize_weights(Tensor w) -> (Tensor, Tensor)");
   m.def("fp8_quantize_weights_both(Tensor w) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("fp8_quantize_rows_cols(Tensor x) -> (Tensor, Tensor, Tensor, Tensor)");
   m.def("signal_flags(Tensor flag_bases, int rank, int seq) -> ()");
   m.def("mm_scatter(Tensor mat_a, Tensor mat_b, Tensor offs, Tensor? bias, Tensor row_ptrs) -> ()");
   m.def("ep_sort(Tensor expert_ids, int num_experts, int topk) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
@@ -1015,6 +1034,7 @@ TORCH_LIBRARY_IMPL(grouped_mm, CUDA, m) {
   m.impl("fp8_quantize_cols", &fp8_quantize_cols_cuda);
   m.impl("fp8_quantize_weights", &fp8_quantize_weights_cuda);
   m.impl("fp8_quantize_weights_both", &fp8_quantize_weights_both_cuda);
+  m.impl("fp8_quantize_rows_cols", &fp8_quantize_rows_cols_cuda);
   m.impl("signal_flags", &signal_flags_cuda);
   m.impl("mm_scatter", &mm_scatter_cuda);
   m.impl("ep_sort", &ep_sort_cuda);

@@ -236,6 +236,10 @@ int mgf_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int64_t ldx
                           void* stream);
 int mgf_fp8_quantize_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq, float* scale,
                           void* stream);
+/* Both scalings of one [rows, cols] activation in two passes: (q_r, s_r) as mgf_fp8_quantize_rows and
+ * (q_c, s_c) as mgf_fp8_quantize_cols give, bit-identical (no counterpart in the reference). */
+int mgf_fp8_quantize_rows_cols(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q_r, int64_t ldq_r,
+                               float* s_r, void* q_c, int64_t ldq_c, float* s_c, void* stream);
 int mgf_fp8_quantize_weights(const void* w, int64_t E, int64_t K, int64_t N, int64_t s_e, int64_t s_k, int64_t s_n,
                              void* q, int64_t ldq, float* scale, void* stream);
 /* Both axes of one weight [E, K, N] (unit stride along n, n % 8 == 0, 16-byte aligned strides and

@@ -197,3 +197,18 @@ def test_fused_both_axes_weight_quantiser_matches_two_calls(shape):
     assert q.shape == r.shape and q_t.shape == r_t.shape
     assert torch.equal(q.view(torch.uint8), r.view(torch.uint8)) and torch.equal(s, rs)
     assert torch.equal(q_t.view(torch.uint8), r_t.view(torch.uint8)) and torch.equal(s_t, rs_t)
+
+
+@pytest.mark.parametrize("shape", [(1029, 2880), (7, 64), (0, 128), (640, 5760), (300, 40)])
+def test_fused_rows_cols_quantiser_matches_two_calls(shape):
+    """quantize_rows_cols(x) gives exactly quantize_rows(x) and quantize_cols(x), bit for bit."""
+    from cutlass_op.bf16_grouped_mm import fp8
+
+    g = torch.Generator().manual_seed(shape[0] + shape[1])
+    x = (torch.randn(*shape, generator=g) * torch.linspace(0.05, 6.0, shape[1])).to(torch.bfloat16).cuda()
+    q_r, s_r, q_c, s_c = fp8.quantize_rows_cols(x)
+    r_r, rs_r = fp8.quantize_rows(x)
+    r_c, rs_c = fp8.quantize_cols(x)
+    torch.cuda.synchronize()
+    assert torch.equal(q_r.view(torch.uint8), r_r.view(torch.uint8)) and torch.equal(s_r, rs_r)
+    assert torch.equal(q_c.view(torch.uint8), r_c.view(torch.uint8)) and torch.equal(s_c, rs_c)
