@@ -1,6 +1,7 @@
 // B200 (sm_100a) grouped GEMM for the MoE FFN path: persistent ragged-M / ragged-K tile
 // scheduler, TMA-fed tcgen05 UMMA with fp32 accumulators in TMEM (double-buffered so the
-// epilogue of tile i overlaps the mainloop of tile i+1), and four fused epilogues:
+// epilogue of tile i overlaps the mainloop of tile i+1, except in the 256-row ragged-K form),
+// and four fused epilogues:
 //   MGF_EPI_BIAS        D = bf16(acc + bias[e])                     (down-proj fwd, dgrads)
 //   MGF_EPI_SWIGLU      aux = bf16(acc + bias[e]), D2 = clamped SwiGLU(aux)  (up-proj fwd)
 //   MGF_EPI_SWIGLU_BWD  D = SwiGLU_bwd(acc, aux)                    (down-proj dgrad)
@@ -24,8 +25,11 @@
 //               TMA tile stores from shared memory (ragged-K)
 //
 // CTA pairs (CG = 2, cluster of two, cta_group::2 MMAs on 256-row tiles) for ragged-M launches whose
-// groups are large; single CTAs (128-row tiles) otherwise and for ragged-K.  F8 = true is the e4m3
-// variant of the ragged-M BIAS / SWIGLU launches (kind::f8f6f4, row-wise scales in the epilogue).
+// groups are large; single CTAs (128-row tiles) otherwise.  Ragged-K runs single CTAs in one of
+// three forms: 256-row tiles (MH = 2: two 128-row accumulators over all of TMEM share each B stage,
+// no TMEM double buffer) for longer groups, one wide TMA store per warp and tile (OB = 4) for short
+// groups, 128-row tiles with 32 x 32 stores otherwise.  F8 = true is the e4m3 variant of every
+// epilogue (kind::f8f6f4, row / column scales applied in the epilogue).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
